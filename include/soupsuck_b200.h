@@ -1,0 +1,191 @@
+/* soupsuck_b200: C ABI of the B200 (sm_100a) QLoRA hot path.
+ *
+ * Every entry point takes raw device pointers, element counts and strides, and
+ * a CUDA stream passed as `void*` (a cudaStream_t; NULL = legacy default
+ * stream).  Nothing here allocates device memory: callers pass outputs and, where
+ * a routine needs scratch space, a workspace whose size the matching
+ * `*_workspace_bytes` query reports.  Every function returns 0 on success or one
+ * of the SB_E* codes; `sb_last_error()` then describes the failure (per thread).
+ * Invalid arguments are rejected before any launch.  No kernel traps the GPU:
+ * a device-side wait that runs out (bounded spin loops) records an error code
+ * that `sb_take_device_error()` reports.
+ *
+ * 16-bit floating-point buffers are IEEE binary16 passed as `uint16_t*`.
+ * Where a routine accepts either binary16 or binary32, a dtype code selects it.
+ *
+ * Reference interface citations are paths inside the Khasuetolog/soupsuck
+ * project; each entry point replaces the Triton launch (or library GEMM) named
+ * beside it.
+ */
+#ifndef SOUPSUCK_B200_H
+#define SOUPSUCK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  SB_OK = 0,
+  SB_EINVAL = 1,       /* unsupported shape, dtype, alignment or NULL pointer */
+  SB_ECUDA = 2,        /* a CUDA runtime call failed */
+  SB_EUNSUPPORTED = 3, /* no kernel for this case on this device */
+  SB_EWORKSPACE = 4    /* workspace smaller than the *_workspace_bytes query */
+};
+
+enum { SB_F16 = 0, SB_F32 = 1 };
+
+/* Library identity and error reporting. */
+int sb_abi_version(void);
+const char* sb_last_error(void);
+/* Reads and clears the device-side error word (bounded-wait timeouts inside the
+ * tcgen05 kernels).  *flag = 0 means no kernel gave up waiting since the last call.
+ * Synchronises `stream`. */
+int sb_take_device_error(void* stream, int* flag);
+/* Number of kernels this library launched since load (a process-wide counter). */
+int64_t sb_launch_count(void);
+
+/* ---------------------------------------------------------------- NF4 decode
+ * Replaces nf4_decode_kernel (solution/kernels/nf4.py:41-59) as launched by
+ * dequantize_nf4 (:190-203, NESTED=True) and _dequantize_flat_into (:181-187,
+ * NESTED=False).  out[i] = fp16_rn(NF4[nib(i)] * scale(i // 64)); bit-exact. */
+int sb_nf4_dequant_nested(const uint8_t* packed, const uint8_t* qabs, const float* absmax2,
+                          const float* code2, const float* offset, uint16_t* out, int64_t n,
+                          void* stream);
+int sb_nf4_dequant_flat(const uint8_t* packed, const float* absmax, uint16_t* out, int64_t n,
+                        void* stream);
+
+/* ---------------------------------------------------------------- NF4 linear
+ * A bitsandbytes nested NF4 weight W[n_out, k_in] (row-major element order,
+ * QuantState.shape = (n_out, k_in)), as validated by _validate_state
+ * (solution/kernels/nf4.py:140-168). */
+typedef struct {
+  const uint8_t* packed;  /* ceil(n_out*k_in/2) bytes, high nibble = earlier element */
+  const uint8_t* qabs;    /* ceil(n_out*k_in/64) uint8 codes into code2 */
+  const float* absmax2;   /* one fp32 scale per 256 blocks */
+  const float* code2;     /* 256 fp32 code values */
+  const float* offset;    /* one fp32 value */
+  int64_t n_out;
+  int64_t k_in;
+} sb_nf4_weight;
+
+/* Forward: Y[m, n_out] = X[m, k_in] . deq(W)^T + lora_a[m, r] . lora_b[n_out, r]^T + bias.
+ * Replaces the base projection (bnb MatMul4Bit -> F.linear, mirrored by
+ * nf4_tile_matmul_kernel TRANSPOSE=False, solution/kernels/nf4_gemm.py:35-71)
+ * plus the LoRA up-projection and lora_scale_add_kernel
+ * (solution/kernels/lora_epilogue.py:24-34) of the patched PEFT forward
+ * (solution/lora.py:135-164).  lora_a is the already-scaled s*(X.A^T) in fp16
+ * (sb_lora_down); pass lora_a = lora_b = NULL, r = 0 for a frozen projection.
+ * X, Y, bias, lora_* are fp16, fp32 accumulation. */
+int sb_nf4_linear_fwd(const uint16_t* x, int64_t m, const sb_nf4_weight* w,
+                      const uint16_t* bias, const uint16_t* lora_a, const uint16_t* lora_b,
+                      int r, uint16_t* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward input gradient: dX[m, k_in] = dY[m, n_out] . deq(W) + lora_a[m, r] . lora_b[k_in, r]^T.
+ * Replaces MatMul4Bit.backward's dequantize + torch.matmul
+ * (solution/nf4_patch.py:62-87, mirrored at solution/kernels/nf4_gemm.py:109-118,
+ * TRANSPOSE=True) plus the LoRA dX term.  lora_a = s*(dY.B) in fp16
+ * (sb_lora_up_grad), lora_b = A^T laid out [k_in, r] (sb_lora_transpose_a). */
+int sb_nf4_linear_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight* w,
+                     const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* dx,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes the two calls above need for these sizes (0 on the tcgen05 path). */
+size_t sb_nf4_linear_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in, int dx);
+
+/* ---------------------------------------------------------------- LoRA factors
+ * The low-rank products around the base projection (nn.Linear under fp16
+ * autocast in solution/lora.py:161, and their autograd backward).  r <= 64. */
+/* z[m, r] = fp16(X . A^T) and zs[m, r] = fp16(scale * X . A^T) (either may be NULL). */
+int sb_lora_down(const uint16_t* x, int64_t m, int64_t k, const uint16_t* a, int r,
+                 float scale, uint16_t* z, uint16_t* zs, void* stream);
+/* u[m, r] = fp16(scale * dY . B) and u32 (fp32, may be NULL); B is [n, r]. */
+int sb_lora_up_grad(const uint16_t* dy, int64_t m, int64_t n, const uint16_t* b, int r,
+                    float scale, uint16_t* u, float* u32, void* stream);
+/* Weight gradients, fp32 accumulation and output, deterministic two-stage
+ * row reduction through `workspace` (sb_lora_grad_workspace_bytes(m, width, r)
+ * bytes, width = k for dA and n for dB):
+ *   da[r, k] = u32^T . X           (u32 = s * dY . B, fp32 [m, r])
+ *   db[n, r] = scale * dY^T . z    (z = X . A^T, fp16 [m, r]) */
+size_t sb_lora_grad_workspace_bytes(int64_t m, int64_t width, int r);
+int sb_lora_grad_a(const float* u32, const uint16_t* x, int64_t m, int64_t k, int r, float* da,
+                   void* workspace, size_t workspace_bytes, void* stream);
+int sb_lora_grad_b(const uint16_t* dy, const uint16_t* z, int64_t m, int64_t n, int r,
+                   float scale, float* db, void* workspace, size_t workspace_bytes,
+                   void* stream);
+/* at[k, r] = a[r, k] (fp16 transpose of lora_A for the dX epilogue term). */
+int sb_lora_transpose_a(const uint16_t* a, int r, int64_t k, uint16_t* at, void* stream);
+
+/* ---------------------------------------------------------------- LoRA epilogue
+ * lora_scale_add_kernel / lora_scale_gradient_kernel
+ * (solution/kernels/lora_epilogue.py:24-43), elementwise, bit-exact. */
+int sb_lora_scale_add(const void* base, int base_dtype, const void* adapter, int adapter_dtype,
+                      void* out, int out_dtype, int64_t count, float scale, int cast_to_base,
+                      void* stream);
+int sb_lora_scale_grad(const void* grad, int grad_dtype, void* dadapter, int adapter_dtype,
+                       int64_t count, float scale, void* stream);
+
+/* ---------------------------------------------------------------- (add-)RMSNorm
+ * add_rmsnorm_forward_kernel / add_rmsnorm_backward_kernel
+ * (solution/kernels/add_rmsnorm.py:37-81) and the Qwen2 RMSNorm kernels
+ * (solution/kernels/rmsnorm.py:42-102).  Rows are contiguous with row stride H
+ * unless a stride argument says otherwise; weight has element stride w_stride.
+ * The sum dtype S = promote(residual, delta); y is stored in y_dtype. */
+int sb_add_rmsnorm_fwd(const void* residual, int r_dtype, const void* delta, int d_dtype,
+                       const void* weight, int w_dtype, int64_t w_stride, void* s, void* y,
+                       int y_dtype, float* rstd, int64_t rows, int64_t h, float eps,
+                       void* stream);
+/* gs / gy may be NULL (no upstream on that output); dr / dd may be NULL. */
+int sb_add_rmsnorm_bwd(const void* s, int s_dtype, const void* weight, int w_dtype,
+                       int64_t w_stride, const float* rstd, const void* gs, int gs_dtype,
+                       int64_t gs_row, int64_t gs_col, const void* gy, int gy_dtype,
+                       int64_t gy_row, int64_t gy_col, void* dr, int dr_dtype, void* dd,
+                       int dd_dtype, int64_t rows, int64_t h, void* stream);
+int sb_rmsnorm_fwd(const void* x, int x_dtype, int64_t x_row, const void* weight, int w_dtype,
+                   int64_t w_stride, void* y, int y_dtype, float* rstd, int64_t rows,
+                   int64_t h, float eps, void* stream);
+int sb_rmsnorm_input_grad(const void* x, int x_dtype, int64_t x_row, const void* weight,
+                          int w_dtype, int64_t w_stride, const void* g, int g_dtype,
+                          int64_t g_row, int64_t g_col, const float* rstd, void* dx,
+                          int64_t rows, int64_t h, void* stream);
+/* Two-stage, atomic-free dgamma = sum_rows(g * cast_X(x * rstd)); when
+ * exact_half != 0 each product is rounded to fp16 first (rmsnorm.py:73-102).
+ * workspace: sb_rmsnorm_weight_grad_workspace_bytes(rows, h). */
+int sb_rmsnorm_weight_grad(const void* x, int x_dtype, int64_t x_row, const void* g,
+                           int g_dtype, int64_t g_row, int64_t g_col, const float* rstd,
+                           void* dw, int dw_dtype, int64_t rows, int64_t h, int exact_half,
+                           void* workspace, size_t workspace_bytes, void* stream);
+size_t sb_rmsnorm_weight_grad_workspace_bytes(int64_t rows, int64_t h);
+
+/* ---------------------------------------------------------------- Fused linear CE
+ * _FrozenLinearCrossEntropy (solution/kernels/cross_entropy.py:133-211):
+ * logits = fp16(hidden . W^T) are formed tile by tile on the tensor cores and
+ * never written to memory.  Forward returns per-row loss (0 where ignored),
+ * entropy, first argmax and lse (fp32 / int64).  hidden fp16 [t, h] row-major;
+ * weight fp16 [v, h] row-major; targets int64 [t]; a target outside [0, v) that
+ * is not ignore_index raises SB_EINVAL from sb_ce_check_targets. */
+int sb_ce_forward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight,
+                  int64_t v, const int64_t* targets, int64_t ignore_index, float* loss,
+                  float* entropy, int64_t* argmax, float* lse, void* workspace,
+                  size_t workspace_bytes, void* stream);
+size_t sb_ce_forward_workspace_bytes(int64_t t, int64_t h, int64_t v);
+/* dhidden[t, h] (dtype dh_dtype) of sum_rows(grad[i] * loss[i]); ignored rows
+ * get exact zeros and never touch their (possibly non-finite) grad. */
+int sb_ce_backward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight,
+                   int64_t v, const int64_t* targets, int64_t ignore_index, const float* lse,
+                   const float* grad, void* dhidden, int dh_dtype, void* workspace,
+                   size_t workspace_bytes, void* stream);
+size_t sb_ce_backward_workspace_bytes(int64_t t, int64_t h, int64_t v);
+/* Host-visible validation of targets (replaces torch._assert_async,
+ * solution/kernels/cross_entropy.py:238-240): *bad = number of targets that
+ * are neither ignore_index nor in [0, v).  Synchronises `stream`. */
+int sb_ce_check_targets(const int64_t* targets, int64_t t, int64_t v, int64_t ignore_index,
+                        int64_t* bad, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOUPSUCK_B200_H */

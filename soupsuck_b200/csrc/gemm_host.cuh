@@ -1,0 +1,140 @@
+// Host side of the tcgen05 GEMM: tensor maps, launch configuration, and the
+// NF4-linear / cross-entropy drivers exported through the C ABI.
+#pragma once
+
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm_sm100.cuh"
+
+namespace sb {
+namespace gemm {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [outer, inner] with a row pitch in bytes; box {box_inner, box_outer}.
+inline int make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                    uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SB_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (!aligned(base, 16) || pitch_bytes % 16 != 0) return fail(SB_EINVAL, "TMA operand not 16-byte aligned");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SB_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return SB_OK;
+}
+
+inline CUtensorMapSwizzle lora_swizzle(int r) {
+  return r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : (r == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int BMODE, int EMODE, int MSUB, int BN, int STAGES>
+int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
+           const CUtensorMap& lb, Params p, cudaStream_t stream, const char* name) {
+  using C = Cfg<BMODE, MSUB, BN, STAGES>;
+  auto kern = gemm_kernel<BMODE, EMODE, MSUB, BN, STAGES>;
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+      if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " smem attribute: " + cudaGetErrorString(e));
+      configured[dev] = true;
+    }
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  if (tiles == 0) return SB_OK;
+  const int sms = device_sm_count();
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(a, b, la, lb, p);
+  count_launch();
+  return check_launch(name);
+}
+
+// ----------------------------------------------------------------- NF4 linear
+constexpr int kNF4Msub = 2, kNF4BN = 128, kNF4Stages = 4;
+
+inline bool nf4_tc_shape_ok(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
+  if (m <= 0 || n_out <= 0 || k_in <= 0) return false;
+  if (k_in % 64 != 0) return false;                  // blocks stay inside weight rows
+  if (dx && (n_out % 8 != 0)) return false;          // dY rows must be 16-byte pitched
+  if (m > 0x7fffffffLL || n_out > 0x7fffffffLL || k_in > 0x7fffffffLL) return false;
+  return true;
+}
+
+inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weight& w,
+                         const uint16_t* bias, const uint16_t* lora_a, const uint16_t* lora_b,
+                         int r, uint16_t* out, cudaStream_t stream) {
+  const int64_t red = dx ? w.n_out : w.k_in;    // reduction length
+  const int64_t width = dx ? w.k_in : w.n_out;  // output columns
+  CUtensorMap ta, tb, tla, tlb;
+  int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, red, m, red * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (!dx) {
+    rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.k_in / 2, w.n_out, w.k_in / 2, 32, kNF4BN,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.k_in / 2, w.n_out, w.k_in / 2, kNF4BN / 2, 64,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (rc) return rc;
+  tla = ta;
+  tlb = ta;
+  if (r > 0) {
+    rc = make_map(&tla, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_a, r, m, r * 2, r, kNF4Msub * 128, lora_swizzle(r));
+    if (rc) return rc;
+    rc = make_map(&tlb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_b, r, width, r * 2, r, kNF4BN, lora_swizzle(r));
+    if (rc) return rc;
+  }
+  Params p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(width);
+  p.K = static_cast<int>(red);
+  p.m_tiles = static_cast<int>((m + kNF4Msub * 128 - 1) / (kNF4Msub * 128));
+  p.n_tiles = static_cast<int>((width + kNF4BN - 1) / kNF4BN);
+  p.k_blocks = static_cast<int>((red + 63) / 64);
+  p.lora_r = r;
+  p.vec_ok = aligned(out, 16) && (width % 8 == 0);
+  p.qabs = w.qabs;
+  p.absmax2 = w.absmax2;
+  p.code2 = w.code2;
+  p.offset = w.offset;
+  p.w_rows = w.n_out;
+  p.w_cols = w.k_in;
+  p.out = out;
+  p.ldo = width;
+  p.bias = reinterpret_cast<const __half*>(bias);
+  if (!dx) {
+    return launch<kNF4Fwd, kStoreF16, kNF4Msub, kNF4BN, kNF4Stages>(ta, tb, tla, tlb, p, stream, "nf4_gemm_fwd");
+  }
+  return launch<kNF4Dx, kStoreF16, kNF4Msub, kNF4BN, kNF4Stages>(ta, tb, tla, tlb, p, stream, "nf4_gemm_dx");
+}
+
+}  // namespace gemm
+}  // namespace sb

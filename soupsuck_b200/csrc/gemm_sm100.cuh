@@ -1,0 +1,578 @@
+// Warp-specialised persistent tcgen05 GEMM for sm_100a with an in-SMEM NF4 decoder.
+//
+//   D[M, N] = A[M, K] . B[N, K]^T  (+ LA[M, r] . LB[N, r]^T)   fp16 x fp16 -> fp32 (TMEM)
+//
+// B comes from one of four sources:
+//   kNF4Fwd   packed NF4 weight W[N, K] (forward Y = X . deq(W)^T): K-major operand;
+//   kNF4Dx    packed NF4 weight W[K_red, N_out] (dX = dY . deq(W)):  MN-major operand;
+//   kDenseK   fp16 B[N, K] row-major (CE logits = hidden . W_head^T);
+//   kDenseMN  fp16 B[K, N] row-major (CE dX = dZ . W_head_chunk).
+// For the NF4 modes the producer TMA-loads the packed bytes (no swizzle) and
+// decoder warps expand them, 64 elements per thread, into the 128B-swizzled fp16
+// layout the UMMA descriptor expects.  The decoded values are bit-identical to
+// the standalone decoder (reference solution/kernels/nf4.py:41-59): per 64-block
+// the thread builds the 16-entry table fp16_rn(NF4[i] * scale) with separate
+// fp32 multiply/add, then expands 8 nibbles at a time with byte permutes.
+//
+// Roles (one CTA per SM; > 114 KB of shared memory so no two tcgen05 kernels
+// share an SM and TMEM allocation never waits on another CTA):
+//   warp 0       TMA producer (A tiles, packed B or dense B, LoRA factors)
+//   warp 1       TMEM allocator + single-thread UMMA issuer
+//   warps 4..7   epilogue (TMEM lanes 32*(warp%4) ..), double-buffered accumulators
+//   warps 8..15  NF4 decoders, two groups of 4 warps alternating k-steps
+// Every mbarrier wait is bounded (common.cuh); on expiry the CTA records an error
+// word, stops issuing, waits (bounded) for its in-flight TMA and UMMA work and
+// frees TMEM before returning.
+//
+// The multiple-of-64 k_in requirement of the NF4 modes keeps each 64-element
+// quantization block inside one weight row, so a tile's block index is
+// row * (k_in / 64) + column / 64; absmax2 is indexed by the global block id.
+#pragma once
+
+#include "common.cuh"
+#include "nf4_dequant.cuh"
+
+namespace sb {
+namespace gemm {
+
+enum BMode : int { kNF4Fwd = 0, kNF4Dx = 1, kDenseK = 2, kDenseMN = 3 };
+enum EMode : int { kStoreF16 = 0, kStoreF32 = 1, kAccF32 = 2, kCeStats = 3, kCeDz = 4 };
+
+constexpr int kBK = 64;        // reduction elements per pipeline stage (one 128 B swizzle row)
+constexpr int kTileRows = 128; // rows per UMMA (M = 128, cta_group::1)
+
+struct Params {
+  int M, N, K;            // logical problem: D[M, N], reduction K
+  int m_tiles, n_tiles, k_blocks;
+  int lora_r;             // 0, 16, 32 or 64: extra LoRA step(s) after the main loop
+  const int* m_dev;       // optional runtime row count (CE backward compaction)
+  int vec_ok;             // output rows are 16-byte aligned
+  // NF4 weight
+  const uint8_t* qabs;
+  const float* absmax2;
+  const float* code2;
+  const float* offset;
+  int64_t w_rows;          // n_out of the weight
+  int64_t w_cols;          // k_in of the weight
+  // epilogue
+  void* out;
+  int64_t ldo;
+  const __half* bias;
+  // cross-entropy epilogues
+  const int64_t* targets;
+  int64_t ignore_index;
+  float* stats;            // kCeStats: [n_tiles, M_alloc, 4] partial (max, sumexp, sumexp*z, target z)
+  int* stats_arg;          // kCeStats: [n_tiles, M_alloc] first argmax (local column)
+  int64_t stats_ld;        // rows of the stats arrays
+  const float* lse;        // kCeDz
+  const float* grad;       // kCeDz: per-row upstream gradient (compacted)
+  const float* gain;       // kCeDz: per-row gain
+  int64_t col_offset;      // vocabulary index of column 0 of this launch
+};
+
+template <int BMODE, int MSUB, int BN, int STAGES>
+struct Cfg {
+  static constexpr bool kNF4 = (BMODE == kNF4Fwd || BMODE == kNF4Dx);
+  static constexpr bool kBMN = (BMODE == kNF4Dx || BMODE == kDenseMN);
+  static constexpr int kABytes = MSUB * kTileRows * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kRawBytes = kNF4 ? BN * kBK / 2 : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+  static constexpr int kTmemCols = 2 * MSUB * BN;
+  static constexpr int kThreads = kNF4 ? 512 : 256;
+  static constexpr int kBarrierBytes = 1024;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 1024;  // + align slack
+  static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
+  static_assert(BN % 64 == 0 && BN <= 256, "BN");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(kSmemBytes > 232448 / 2, "one CTA per SM keeps TMEM allocation uncontended");
+};
+
+// ------------------------------------------------------------ NF4 decode (SMEM)
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Expand 8 NF4 codes (one packed word) through the per-block table into 8 fp16.
+// L/H hold the low/high bytes of table entries 0..15.  Entries 0-7 and 8-15 are
+// looked up separately with 3-bit selectors, then merged on bit 3 of each code.
+__device__ __forceinline__ uint4 nf4_expand8(uint32_t w, const uint32_t (&L)[4],
+                                             const uint32_t (&H)[4]) {
+  uint4 o;
+  {
+    const uint32_t s = w & 0x7777u;
+    const uint32_t sel = ((w >> 1) & 0x4444u) | 0x3210u;
+    const uint32_t lo = prmt(prmt(L[0], L[1], s), prmt(L[2], L[3], s), sel);
+    const uint32_t hi = prmt(prmt(H[0], H[1], s), prmt(H[2], H[3], s), sel);
+    o.x = prmt(lo, hi, 0x4051u);  // elements 0, 1 (high nibble of byte 0 first)
+    o.y = prmt(lo, hi, 0x6273u);  // elements 2, 3
+  }
+  {
+    const uint32_t u = w >> 16;
+    const uint32_t s = u & 0x7777u;
+    const uint32_t sel = ((u >> 1) & 0x4444u) | 0x3210u;
+    const uint32_t lo = prmt(prmt(L[0], L[1], s), prmt(L[2], L[3], s), sel);
+    const uint32_t hi = prmt(prmt(H[0], H[1], s), prmt(H[2], H[3], s), sel);
+    o.z = prmt(lo, hi, 0x4051u);
+    o.w = prmt(lo, hi, 0x6273u);
+  }
+  return o;
+}
+
+__device__ __forceinline__ void nf4_table(float scale, uint32_t (&L)[4], uint32_t (&H)[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    __half2 h01 = __floats2half2_rn(__fmul_rn(c_nf4_values[4 * q], scale),
+                                    __fmul_rn(c_nf4_values[4 * q + 1], scale));
+    __half2 h23 = __floats2half2_rn(__fmul_rn(c_nf4_values[4 * q + 2], scale),
+                                    __fmul_rn(c_nf4_values[4 * q + 3], scale));
+    const uint32_t a = *reinterpret_cast<uint32_t*>(&h01);
+    const uint32_t b = *reinterpret_cast<uint32_t*>(&h23);
+    L[q] = prmt(a, b, 0x6420u);
+    H[q] = prmt(a, b, 0x7531u);
+  }
+}
+
+// Decode one 64-element block (32 packed bytes at `raw`) into a 128-byte
+// swizzled SMEM row at `dst` (row index `r` inside its 8-row swizzle atom).
+__device__ __forceinline__ void nf4_decode_row(const uint8_t* raw, uint8_t* dst, int r,
+                                               float scale, bool valid) {
+  const uint32_t swz = static_cast<uint32_t>(r & 7);
+  if (!valid) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      *reinterpret_cast<uint4*>(dst + ((c ^ swz) << 4)) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  const uint4 p0 = *reinterpret_cast<const uint4*>(raw);
+  const uint4 p1 = *reinterpret_cast<const uint4*>(raw + 16);
+  uint32_t L[4], H[4];
+  nf4_table(scale, L, H);
+  const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    *reinterpret_cast<uint4*>(dst + ((c ^ swz) << 4)) = nf4_expand8(words[c], L, H);
+  }
+}
+
+__device__ __forceinline__ float nf4_scale(const Params& p, int64_t blk, float off) {
+  const float code = __ldg(p.code2 + __ldg(p.qabs + blk));
+  return __fadd_rn(__fmul_rn(code, __ldg(p.absmax2 + (blk >> 8))), off);
+}
+
+// ------------------------------------------------------------ epilogue helpers
+__device__ __forceinline__ int runtime_rows(const Params& p) {
+  return p.m_dev ? *p.m_dev : p.M;
+}
+
+// Per-row epilogue state carried across the 32-column chunks of one tile.
+struct EpiState {
+  float m, s, t, tz;   // CE stats: running max, sum exp(z-m), sum exp(z-m)*z, target logit
+  int arg;             // CE stats: first argmax (column within this launch)
+  int64_t tgt;         // target vocabulary index (or ignore_index)
+  float lse, gscale;   // CE dz: row lse and g / gain
+};
+
+__device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
+
+template <int EMODE>
+__device__ __forceinline__ void epilogue_begin(const Params& p, EpiState& st, int row, int rows_valid) {
+  if constexpr (EMODE == kCeStats) {
+    st.m = -INFINITY; st.s = 0.0f; st.t = 0.0f; st.tz = 0.0f; st.arg = 0x7fffffff;
+    st.tgt = row < rows_valid ? p.targets[row] : p.ignore_index;
+  } else if constexpr (EMODE == kCeDz) {
+    st.tgt = p.ignore_index; st.lse = 0.0f; st.gscale = 0.0f;
+    if (row < rows_valid) {
+      st.tgt = p.targets[row];
+      st.lse = p.lse[row];
+      st.gscale = __fdiv_rn(p.grad[row], p.gain[row]);
+    }
+  }
+}
+
+template <int EMODE>
+__device__ __forceinline__ void epilogue_chunk(const Params& p, EpiState& st, const uint32_t (&v)[32],
+                                               int row, int col0, int rows_valid) {
+  if constexpr (EMODE == kCeStats) {
+    // Logits are the fp16-rounded GEMM result (reference: torch.mm with fp16 output,
+    // solution/kernels/cross_entropy.py:149); statistics follow :57-89.
+    float z[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) z[j] = (col0 + j < p.N) ? round_f16(__uint_as_float(v[j])) : -INFINITY;
+    float cmax = z[0];
+    int carg = 0;
+#pragma unroll
+    for (int j = 1; j < 32; ++j) {
+      if (z[j] > cmax) { cmax = z[j]; carg = j; }
+    }
+    if (cmax > st.m) {
+      const float r = st.m == -INFINITY ? 0.0f : __expf(st.m - cmax);
+      st.s *= r;
+      st.t *= r;
+      st.m = cmax;
+      st.arg = col0 + carg;
+    }
+    if (st.m != -INFINITY) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) {
+          const float e = __expf(z[j] - st.m);
+          st.s += e;
+          st.t = fmaf(e, z[j], st.t);
+        }
+      }
+    }
+    const int64_t g0 = p.col_offset + col0;
+    if (st.tgt != p.ignore_index && st.tgt >= g0 && st.tgt < g0 + 32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (g0 + j == st.tgt && col0 + j < p.N) st.tz = z[j];
+      }
+    }
+  } else if constexpr (EMODE == kCeDz) {
+    // dz = fp16((exp(z - lse) - onehot) * g / gain)  (solution/kernels/cross_entropy.py:108-122).
+    if (row >= rows_valid) return;
+    __half* out = static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+    const int64_t g0 = p.col_offset + col0;
+    float d[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float e = __expf(round_f16(__uint_as_float(v[j])) - st.lse);
+      if (g0 + j == st.tgt) e -= 1.0f;
+      d[j] = e * st.gscale;
+    }
+    if (p.vec_ok && col0 + 32 <= p.N) {
+      uint32_t h[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        __half2 t = __floats2half2_rn(d[2 * j], d[2 * j + 1]);
+        h[j] = *reinterpret_cast<uint32_t*>(&t);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + col0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+    } else {
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) out[col0 + j] = __float2half_rn(d[j]);
+      }
+    }
+  } else if constexpr (EMODE == kStoreF16) {
+    if (row >= rows_valid) return;
+    __half* out = static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+    float f[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+    if (p.bias) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) f[j] = __fadd_rn(f[j], __half2float(p.bias[col0 + j]));
+      }
+    }
+    if (p.vec_ok && col0 + 32 <= p.N) {
+      uint32_t h[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        __half2 t = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+        h[j] = *reinterpret_cast<uint32_t*>(&t);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + col0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+    } else {
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) out[col0 + j] = __float2half_rn(f[j]);
+      }
+    }
+  } else {  // kStoreF32 / kAccF32
+    if (row >= rows_valid) return;
+    float* out = static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+    if (p.vec_ok && col0 + 32 <= p.N) {
+      float4* dst = reinterpret_cast<float4*>(out + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 a = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                               __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+        if constexpr (EMODE == kAccF32) {
+          const float4 o = dst[j];
+          a.x += o.x; a.y += o.y; a.z += o.z; a.w += o.w;
+        }
+        dst[j] = a;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) {
+          const float a = __uint_as_float(v[j]);
+          if constexpr (EMODE == kAccF32) out[col0 + j] += a; else out[col0 + j] = a;
+        }
+      }
+    }
+  }
+}
+
+template <int EMODE>
+__device__ __forceinline__ void epilogue_end(const Params& p, const EpiState& st, int row, int nt,
+                                             int rows_valid) {
+  if constexpr (EMODE == kCeStats) {
+    if (row < rows_valid) {
+      const int64_t ld = p.stats_ld;
+      float* base = p.stats + static_cast<int64_t>(nt) * 4 * ld + row;
+      base[0] = st.m;
+      base[ld] = st.s;
+      base[2 * ld] = st.t;
+      base[3 * ld] = st.tz;
+      p.stats_arg[static_cast<int64_t>(nt) * ld + row] = st.arg;
+    }
+  }
+}
+
+// ------------------------------------------------------------ the kernel
+template <int BMODE, int EMODE, int MSUB, int BN, int STAGES>
+__global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
+                const Params p) {
+  using C = Cfg<BMODE, MSUB, BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bar_area = smem + STAGES * C::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty = full + STAGES;
+  uint64_t* decoded = empty + STAGES;
+  uint64_t* acc_full = decoded + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+  const int steps = p.k_blocks + (p.lora_r > 0 ? 1 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&decoded[s], 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::kTmemCols);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      if (p.lora_r > 0) {
+        tma_prefetch_desc(&tmLA);
+        tma_prefetch_desc(&tmLB);
+      }
+      const int rows_valid = runtime_rows(p);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+        const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
+        if (m0 >= rows_valid) continue;
+        for (int step = 0; step < steps; ++step, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) { ok = false; break; }
+          uint8_t* a_s = smem + s * C::kStageBytes;
+          uint8_t* b_s = a_s + C::kABytes;
+          uint8_t* raw_s = b_s + C::kBBytes;
+          if (step < p.k_blocks) {
+            mbar_arrive_expect_tx(&full[s], C::kABytes + (C::kNF4 ? C::kRawBytes : C::kBBytes));
+#pragma unroll
+            for (int ms = 0; ms < MSUB; ++ms) {
+              tma_load_2d(a_s + ms * kTileRows * kBK * 2, &tmA, &full[s], step * kBK, m0 + ms * kTileRows);
+            }
+            if constexpr (BMODE == kNF4Fwd) {
+              tma_load_2d(raw_s, &tmB, &full[s], step * (kBK / 2), n0);
+            } else if constexpr (BMODE == kNF4Dx) {
+              tma_load_2d(raw_s, &tmB, &full[s], n0 / 2, step * kBK);
+            } else if constexpr (BMODE == kDenseK) {
+              tma_load_2d(b_s, &tmB, &full[s], step * kBK, n0);
+            } else {
+#pragma unroll
+              for (int pnl = 0; pnl < BN / 64; ++pnl) {
+                tma_load_2d(b_s + pnl * 64 * 128, &tmB, &full[s], n0 + pnl * 64, step * kBK);
+              }
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[s], (MSUB * kTileRows + BN) * p.lora_r * 2);
+            tma_load_2d(a_s, &tmLA, &full[s], 0, m0);
+            tma_load_2d(b_s, &tmLB, &full[s], 0, n0);
+          }
+        }
+      }
+      // Drain: every TMA this thread issued must land before the CTA exits.
+      const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0;
+      for (uint32_t j = first; j < it; ++j) {
+        volatile int no_abort = 0;
+        mbar_wait(&full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_f16_f32(kTileRows, BN, 0, C::kBMN ? 1 : 0);
+      constexpr uint32_t kIdescLora = idesc_f16_f32(kTileRows, BN, 0, 0);
+      const uint32_t lora_layout = p.lora_r == 16 ? kSwizzle32B : (p.lora_r == 32 ? kSwizzle64B : kSwizzle128B);
+      const uint32_t lora_pitch = static_cast<uint32_t>(p.lora_r) * 2;
+      const int rows_valid = runtime_rows(p);
+      uint32_t it = 0, tl = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if ((tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
+        const int buf = tl & 1;
+        const uint32_t aph = (tl >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + buf * MSUB * BN;
+        for (int step = 0; step < steps; ++step, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
+          if (C::kNF4 && step < p.k_blocks) {
+            if (!mbar_wait(&decoded[s], ph, kErrWaitDecoded, abort_flag)) { ok = false; break; }
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(smem + s * C::kStageBytes);
+          const uint32_t b_addr = a_addr + C::kABytes;
+          if (step < p.k_blocks) {
+#pragma unroll
+            for (int k16 = 0; k16 < kBK / 16; ++k16) {
+              const uint64_t bdesc = C::kBMN
+                  ? smem_desc(b_addr + k16 * 16 * 128, 64 * 128, 1024, kSwizzle128B)
+                  : smem_desc(b_addr + k16 * 32, 16, 1024, kSwizzle128B);
+#pragma unroll
+              for (int ms = 0; ms < MSUB; ++ms) {
+                const uint64_t adesc = smem_desc(a_addr + ms * kTileRows * kBK * 2 + k16 * 32, 16, 1024, kSwizzle128B);
+                umma_f16(acc + ms * BN, adesc, bdesc, kIdesc, (step > 0 || k16 > 0) ? 1u : 0u);
+              }
+            }
+          } else {
+            for (int k16 = 0; k16 < p.lora_r / 16; ++k16) {
+              const uint64_t bdesc = smem_desc(b_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
+#pragma unroll
+              for (int ms = 0; ms < MSUB; ++ms) {
+                const uint64_t adesc = smem_desc(a_addr + ms * kTileRows * lora_pitch + k16 * 32, 16,
+                                                 8 * lora_pitch, lora_layout);
+                umma_f16(acc + ms * BN, adesc, bdesc, kIdescLora, 1u);
+              }
+            }
+          }
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+        ++tl;
+      }
+      // Drain: wait for every UMMA issued above before TMEM is freed.
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, kErrWaitDrain, &no_abort);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int rows_valid = runtime_rows(p);
+    uint32_t tl = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+      const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
+      if (m0 >= rows_valid) continue;
+      const int buf = tl & 1;
+      const uint32_t aph = (tl >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int ms = 0; ms < MSUB; ++ms) {
+        const int row = m0 + ms * kTileRows + q * 32 + lane;
+        EpiState st;
+        epilogue_begin<EMODE>(p, st, row, rows_valid);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * MSUB * BN + ms * BN + c * 32, v);
+          tmem_ld_wait();
+          epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+        }
+        epilogue_end<EMODE>(p, st, row, nt, rows_valid);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      ++tl;
+    }
+  } else if (C::kNF4 && warp >= 8) {
+    // ------------------------------------------------------------ NF4 decoders
+    const int group = (warp - 8) >> 2;
+    const int gtid = ((warp - 8) & 3) * 32 + lane;
+    const float off = __ldg(p.offset);
+    const int64_t bpr = p.w_cols / 64;
+    const int rows_valid = runtime_rows(p);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      if ((tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
+      const int nt = tile / p.m_tiles;
+      const int n0 = nt * BN;
+      for (int step = 0; step < steps; ++step, ++it) {
+        if (static_cast<int>(it & 1) != group) continue;
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
+        if (step < p.k_blocks) {
+          uint8_t* b_s = smem + s * C::kStageBytes + C::kABytes;
+          const uint8_t* raw_s = b_s + C::kBBytes;
+#pragma unroll
+          for (int task = gtid; task < BN; task += 128) {
+            if constexpr (BMODE == kNF4Fwd) {
+              const int r = task;
+              const int64_t wrow = n0 + r;
+              const bool valid = wrow < p.w_rows;
+              const float scale = valid ? nf4_scale(p, wrow * bpr + step, off) : 0.0f;
+              nf4_decode_row(raw_s + r * 32, b_s + r * 128, r, scale, valid);
+            } else {
+              constexpr int kPanels = BN / 64;
+              const int r = task / kPanels, j = task % kPanels;
+              const int64_t wrow = static_cast<int64_t>(step) * kBK + r;
+              const int64_t wcol = n0 + 64 * j;
+              const bool valid = wrow < p.w_rows && wcol < p.w_cols;
+              const float scale = valid ? nf4_scale(p, wrow * bpr + wcol / 64, off) : 0.0f;
+              nf4_decode_row(raw_s + r * (BN / 2) + j * 32, b_s + j * (kBK * 128) + r * 128, r, scale, valid);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&decoded[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace gemm
+}  // namespace sb

@@ -1,0 +1,9 @@
+// Unity build of libsoupsuck_b200.so: every component is one translation unit,
+// so the device error word and constant tables need no relocatable device code.
+#include "runtime.cuh"
+#include "nf4_dequant.cuh"
+#include "rowwise.cuh"
+#include "gemm_sm100.cuh"
+#include "gemm_host.cuh"
+#include "linear.cuh"
+#include "cross_entropy.cuh"
