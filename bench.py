@@ -1,0 +1,505 @@
+"""Benchmark of the B200 QLoRA hot path (driver contract: one JSON line on rank 0).
+
+Workload: one Qwen2.5-1.5B decoder layer's seven NF4
+projections (q 1536->1536, k/v 1536->256, o 1536->1536, gate/up 1536->8960,
+down 8960->1536), NF4/block64 + double-quant/block256 weights ~N(0, 0.02),
+LoRA r=16 alpha=32 on every projection, T=3300 packed fp16 tokens ~N(0, 1),
+fused residual add-RMSNorm (eps 1e-6, gamma ~N(1, 0.1)) before attention and
+before the MLP, forward plus backward (dX of every projection, LoRA dA/dB,
+norm gradients).  Attention and SwiGLU are outside the hot path: their outputs
+are synthetic inputs of o_proj / down_proj and their upstream gradients are
+synthetic too.  One step = that layer forward + backward on one micro-batch.
+
+value     = algorithmic NF4-GEMM FLOPs of the step (fwd 2MNK+2MKr+2MrN,
+            dX 2MNK+2MNr+2MrK per projection) / device time, whole job;
+e2e       = the same through the public API with every input copied from
+            pinned host memory and the layer-input gradient read back;
+roofline  = the fused NF4 GEMM (dominant kernel) timed alone with CUDA events
+            against the measured dense bf16 peak;
+ce        = fused linear CE fwd+bwd tokens/s at configs[3] (T=3300,
+            V=151936, H=1536, 63% ignored);
+cpu_baseline = the reference's path restated on the host (oracle/cpu_path.py).
+
+Multi-GPU (torchrun, NCCL): each rank runs its own micro-batch (data parallel,
+weak scaling) and the LoRA gradients are all-reduced every step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HIDDEN, INTER, KV = 1536, 8960, 256
+RANK_R, ALPHA = 16, 32
+T_TOKENS = 3300
+EPS = 1e-6
+PROJ = [("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN), ("o", HIDDEN, HIDDEN),
+        ("gate", INTER, HIDDEN), ("up", INTER, HIDDEN), ("down", HIDDEN, INTER)]
+METRIC = "NF4 dequant-GEMM TFLOP/s (% peak) fwd+bwd at Qwen2.5-1.5B shapes; CE tokens/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def proj_flops(m, n, k, r):
+    fwd = 2 * m * n * k + 2 * m * k * r + 2 * m * r * n
+    dx = 2 * m * n * k + 2 * m * n * r + 2 * m * r * k
+    return fwd, dx
+
+
+def step_flops(m):
+    return sum(sum(proj_flops(m, n, k, RANK_R)) for _, n, k in PROJ)
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event (throttle) reasons through NVML every
+    10 ms in a background thread while the timed region runs (read-only)."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
+
+    def __init__(self, index, period=0.01):
+        self.index, self.period = index, period
+        self.samples, self.max_mhz, self.reasons = [], None, set()
+
+    def _run(self):
+        import pynvml
+        h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+            mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+            for name, bit in self.REASONS.items():
+                if mask & bit:
+                    self.reasons.add(name)
+            self.stop.wait(self.period)
+
+    def __enter__(self):
+        import threading
+        self.stop = threading.Event()
+        self.thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.thread = None
+        return self
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ layer
+def build_layer(torch, device, seed):
+    from soupsuck_b200.quantize import quantize_nf4
+    g = torch.Generator(device=device).manual_seed(seed)
+    layer = {}
+    for name, n, k in PROJ:
+        w = (torch.randn((n, k), device=device, generator=g) * 0.02).to(torch.float16)
+        packed, st = quantize_nf4(w)
+        a = ((torch.rand((RANK_R, k), device=device, generator=g) * 2 - 1) / math.sqrt(k)).requires_grad_()
+        b = (torch.randn((n, RANK_R), device=device, generator=g) * 0.01).requires_grad_()
+        layer[name] = (packed, st, a, b)
+    layer["gamma_in"] = (1 + 0.1 * torch.randn(HIDDEN, device=device, generator=g)).to(torch.float16)
+    layer["gamma_post"] = (1 + 0.1 * torch.randn(HIDDEN, device=device, generator=g)).to(torch.float16)
+    return layer
+
+
+def input_shapes(t):
+    return {"residual": (t, HIDDEN), "mlp_prev": (t, HIDDEN), "attn": (t, HIDDEN), "act": (t, INTER),
+            "g_q": (t, HIDDEN), "g_k": (t, KV), "g_v": (t, KV), "g_gate": (t, INTER),
+            "g_up": (t, INTER), "g_out": (t, HIDDEN)}
+
+
+def layer_step(torch, layer, inp):
+    """Forward + backward of the hot path of one decoder layer (public API calls)."""
+    from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear
+    s = ALPHA / RANK_R
+
+    def proj(name, x):
+        packed, st, a, b = layer[name]
+        return nf4_lora_linear(x, packed, st, a, b, s)
+
+    s1, y1 = add_rms_norm(inp["residual"], inp["mlp_prev"], layer["gamma_in"], EPS)
+    q, k, v = proj("q", y1), proj("k", y1), proj("v", y1)
+    o = proj("o", inp["attn"])
+    s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
+    gate, up = proj("gate", y2), proj("up", y2)
+    down = proj("down", inp["act"])
+    out = s2 + down
+    torch.autograd.backward([q, k, v, gate, up, out],
+                            [inp["g_q"], inp["g_k"], inp["g_v"], inp["g_gate"], inp["g_up"], inp["g_out"]])
+    return inp["residual"].grad
+
+
+def lora_params(layer):
+    ps = []
+    for name, _, _ in PROJ:
+        ps.extend(layer[name][2:4])
+    return ps
+
+
+# ------------------------------------------------------------------ CPU reference
+def run_cpu_sample(torch, layer, budget_s):
+    from oracle.cpu_path import CpuProjection, threads, time_projections
+    projs = [CpuProjection(layer[name][0], layer[name][1], layer[name][2], layer[name][3],
+                           ALPHA / RANK_R) for name, _, _ in PROJ]
+    rows = 128
+    sec, flops = time_projections(projs, rows, budget_s=budget_s)
+    return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": threads(), "kind": "port",
+            "sample": f"fwd+dX of the 7 projections on {rows} of {T_TOKENS} rows per pass "
+                      f"(dequant via C oracle on {threads()} threads + torch fp32 matmul), "
+                      f"{sec:.3f} s per pass"}
+
+
+def run_reference(args, torch):
+    """--impl reference: the reference's CPU path (oracle port), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    layer = build_layer(torch, "cpu", seed=0)
+    from oracle.cpu_path import CpuProjection, threads, time_projections
+    projs = [CpuProjection(layer[name][0], layer[name][1], layer[name][2], layer[name][3],
+                           ALPHA / RANK_R) for name, _, _ in PROJ]
+    rows = 128
+    time_projections(projs, rows, budget_s=0.0, min_reps=max(1, min(args.warmup, 1)))
+    per = []
+    flops = None
+    for _ in range(args.steps):
+        sec, flops = time_projections(projs, rows, budget_s=0.0, min_reps=1)
+        per.append(sec)
+    total = sum(per)
+    value = flops * len(per) / total / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * total / len(per), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"configs[1] sample: 7 NF4+LoRA projections fwd+dX, {rows} of "
+                                   f"{T_TOKENS} rows per step", "tokens": rows},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads(), "kind": "port",
+                             "sample": f"{rows} rows x 7 projections fwd+dX per step"},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU timing helpers
+def gemm_roofline(torch, layer, device, t):
+    """Time the fused NF4 GEMM launches of one step (forward and dX of all seven
+    projections, LoRA fused) back to back with CUDA events on their stream."""
+    from soupsuck_b200.kernels.nf4_gemm import nf4_linear_raw
+    calls = []
+    flops = 0
+    for name, n, k in PROJ:
+        packed, st, a, b = layer[name]
+        x = torch.randn((t, k), device=device, dtype=torch.float16)
+        dy = torch.randn((t, n), device=device, dtype=torch.float16)
+        za = torch.randn((t, RANK_R), device=device, dtype=torch.float16)
+        bt = b.detach().half().contiguous()
+        at = a.detach().half().t().contiguous()
+        calls.append(lambda x=x, p=packed, s=st, za=za, bt=bt: nf4_linear_raw(x, p, s, lora_a=za, lora_b=bt))
+        calls.append(lambda dy=dy, p=packed, s=st, za=za, at=at: nf4_linear_raw(dy, p, s, transpose=True, lora_a=za, lora_b=at))
+        f, d = proj_flops(t, n, k, RANK_R)
+        flops += f + d
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        for c in calls:
+            c()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    times = []
+    for _ in range(10):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for c in calls:
+            c()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) / 1000.0)
+    sec = statistics.median(times)
+    return flops, sec, len(calls)
+
+
+def ce_benchmark(torch, device, steps):
+    from soupsuck_b200.kernels import fused_linear_cross_entropy
+    t, h, v = T_TOKENS, HIDDEN, 151936
+    g = torch.Generator(device=device).manual_seed(4)
+    hidden = torch.randn((t, h), device=device, dtype=torch.float16, generator=g).requires_grad_()
+    weight = (torch.randn((v, h), device=device, generator=g) * 0.02).to(torch.float16)
+    targets = torch.randint(v, (t,), device=device, generator=g)
+    mask = torch.rand(t, device=device, generator=g) < 0.63
+    targets[mask] = -100
+    valid = int((targets != -100).sum().item())
+
+    def once():
+        loss = fused_linear_cross_entropy(hidden, weight, targets, validate=False)[0]
+        loss.sum().backward()
+        hidden.grad = None
+
+    for _ in range(2):
+        once()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(max(3, min(steps, 10))):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        once()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) / 1000.0)
+    sec = statistics.median(times)
+    flops = 2 * t * v * h + 4 * valid * v * h
+    return {"tokens_per_s": t / sec, "ms_per_step": 1000 * sec, "tflops": flops / sec / 1e12,
+            "config": {"tokens": t, "vocab": v, "hidden": h, "labelled": valid}}
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=T_TOKENS)
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ce", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+
+    import torch
+
+    if args.impl == "reference":
+        return run_reference(args, torch)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    from soupsuck_b200 import _lib
+    t = args.tokens
+    layer = build_layer(torch, device, seed=0)
+    params = lora_params(layer)
+    shapes = input_shapes(t)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    dev_in = {}
+    for name, shp in shapes.items():
+        dev_in[name] = torch.randn(shp, device=device, dtype=torch.float16, generator=g)
+    for name in ("residual", "attn", "act", "mlp_prev"):
+        dev_in[name].requires_grad_()
+    flat_grad = None
+
+    def zero_grads():
+        for p in params:
+            p.grad = None
+        for name in ("residual", "attn", "act", "mlp_prev"):
+            dev_in[name].grad = None
+
+    def allreduce_grads():
+        nonlocal flat_grad
+        if dist is None:
+            return
+        grads = [p.grad for p in params]
+        flat = torch.cat([gr.reshape(-1) for gr in grads])
+        dist.all_reduce(flat)
+        flat.div_(world)
+        off = 0
+        for p in params:
+            n = p.numel()
+            p.grad.copy_(flat[off:off + n].view_as(p))
+            off += n
+
+    def device_step():
+        zero_grads()
+        layer_step(torch, layer, dev_in)
+        allreduce_grads()
+
+    # Warm-up (also configures kernels before any capture).
+    for _ in range(max(args.warmup, 3)):
+        device_step()
+    torch.cuda.synchronize()
+
+    graph = None
+    launches_per_step = None
+    if not args.no_graph:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                device_step()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        zero_grads()
+        before = _lib.launch_count()
+        with torch.cuda.graph(graph):
+            layer_step(torch, layer, dev_in)
+        launches_per_step = _lib.launch_count() - before
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+
+    def run_step():
+        # With a graph the LoRA gradients live in the graph's pool and are
+        # overwritten by every replay; the all-reduce stays outside the graph.
+        if graph is not None:
+            graph.replay()
+            allreduce_grads()
+        else:
+            device_step()
+
+    if launches_per_step is None:
+        before = _lib.launch_count()
+        run_step()
+        torch.cuda.synchronize()
+        launches_per_step = _lib.launch_count() - before
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    # ---- timed region: K steps, L2 flushed before each (outside the events)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    step_times = []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run_step()
+            e1.record(stream)
+            e1.synchronize()
+            step_times.append(e0.elapsed_time(e1) / 1000.0)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    local_total = sum(step_times)
+    total = local_total
+    if dist is not None:
+        tt = torch.tensor([local_total], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total = float(tt.item())
+    sec_per_step = total / args.steps
+    flops = step_flops(t) * world
+    value = flops / sec_per_step / 1e12
+    dev_err = _lib.take_device_error(device)
+
+    # ---- end-to-end through the public API with host buffers
+    host = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in dev_in.items()}
+    for k in host:
+        host[k].copy_(dev_in[k].detach())
+    out_host = torch.empty((t, HIDDEN), dtype=torch.float16, pin_memory=True)
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        for k, hv in host.items():
+            with torch.no_grad():
+                dev_in[k].copy_(hv, non_blocking=True)
+        run_step()
+        out_host.copy_(dev_in["residual"].grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e2e_times = []
+    for _ in range(max(3, min(args.steps, 10))):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        e2e_step()
+        e1.record(stream)
+        e1.synchronize()
+        e2e_times.append(e0.elapsed_time(e1) / 1000.0)
+    e2e_local = sum(e2e_times) / len(e2e_times)
+    e2e_sec = e2e_local
+    if dist is not None:
+        tt = torch.tensor([e2e_local], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_sec = float(tt.item())
+    e2e_value = flops / e2e_sec / 1e12
+
+    if rank != 0:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    peak_burst, peak_sust, hbm, peak_kind = measured_peaks()
+    gflops, gsec, glaunch = gemm_roofline(torch, layer, device, t)
+    achieved = gflops / gsec / 1e12
+    ce = None if args.no_ce else ce_benchmark(torch, device, args.steps)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu_sample(torch, layer, args.cpu_budget)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * sec_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) NF4 weights)",
+        "config": {"workload": "configs[1]: Qwen2.5-1.5B layer, 7 NF4+LoRA(r=16) projections + 2 add-RMSNorm, fwd+bwd",
+                   "tokens_per_gpu": t, "global_tokens": t * world,
+                   "parallelism": f"dp{world}" + (" + LoRA-grad NCCL all-reduce" if world > 1 else ""),
+                   "l2": "flushed (256 MiB write) before every timed step, outside the events",
+                   "cuda_graph": graph is not None},
+        "pct_peak": 100.0 * value / peak_burst,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": 1000 * e2e_sec},
+        "gpu_launches": int(launches_per_step) * args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_burst, "unit": "TFLOP/s",
+                     "frac": achieved / peak_burst, "traffic": None,
+                     "kernel": "gemm_kernel<NF4> fwd+dX, LoRA fused",
+                     "peak_source": f"{peak_kind} bf16 dense burst (MEASURED_PEAKS.json)",
+                     "launches": glaunch, "ms_per_pass": 1000 * gsec},
+        "clocks": clocks.summary(),
+        "device_error": dev_err,
+    }
+    if ce is not None:
+        line["ce"] = ce
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

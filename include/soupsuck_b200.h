@@ -77,7 +77,7 @@ typedef struct {
  * plus the LoRA up-projection and lora_scale_add_kernel
  * (solution/kernels/lora_epilogue.py:24-34) of the patched PEFT forward
  * (solution/lora.py:135-164).  lora_a is the already-scaled s*(X.A^T) in fp16
- * (sb_lora_down); pass lora_a = lora_b = NULL, r = 0 for a frozen projection.
+ * (sb_lora_project); pass lora_a = lora_b = NULL, r = 0 for a frozen projection.
  * X, Y, bias, lora_* are fp16, fp32 accumulation. */
 int sb_nf4_linear_fwd(const uint16_t* x, int64_t m, const sb_nf4_weight* w,
                       const uint16_t* bias, const uint16_t* lora_a, const uint16_t* lora_b,
@@ -87,7 +87,7 @@ int sb_nf4_linear_fwd(const uint16_t* x, int64_t m, const sb_nf4_weight* w,
  * Replaces MatMul4Bit.backward's dequantize + torch.matmul
  * (solution/nf4_patch.py:62-87, mirrored at solution/kernels/nf4_gemm.py:109-118,
  * TRANSPOSE=True) plus the LoRA dX term.  lora_a = s*(dY.B) in fp16
- * (sb_lora_up_grad), lora_b = A^T laid out [k_in, r] (sb_lora_transpose_a). */
+ * (sb_lora_project), lora_b = A^T laid out [k_in, r] (sb_lora_prepare). */
 int sb_nf4_linear_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight* w,
                      const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* dx,
                      void* workspace, size_t workspace_bytes, void* stream);
@@ -96,27 +96,31 @@ int sb_nf4_linear_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight* w,
 size_t sb_nf4_linear_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in, int dx);
 
 /* ---------------------------------------------------------------- LoRA factors
- * The low-rank products around the base projection (nn.Linear under fp16
- * autocast in solution/lora.py:161, and their autograd backward).  r <= 64. */
-/* z[m, r] = fp16(X . A^T) and zs[m, r] = fp16(scale * X . A^T) (either may be NULL). */
-int sb_lora_down(const uint16_t* x, int64_t m, int64_t k, const uint16_t* a, int r,
-                 float scale, uint16_t* z, uint16_t* zs, void* stream);
-/* u[m, r] = fp16(scale * dY . B) and u32 (fp32, may be NULL); B is [n, r]. */
-int sb_lora_up_grad(const uint16_t* dy, int64_t m, int64_t n, const uint16_t* b, int r,
-                    float scale, uint16_t* u, float* u32, void* stream);
-/* Weight gradients, fp32 accumulation and output, deterministic two-stage
- * row reduction through `workspace` (sb_lora_grad_workspace_bytes(m, width, r)
- * bytes, width = k for dA and n for dB):
- *   da[r, k] = u32^T . X           (u32 = s * dY . B, fp32 [m, r])
- *   db[n, r] = scale * dY^T . z    (z = X . A^T, fp16 [m, r]) */
-size_t sb_lora_grad_workspace_bytes(int64_t m, int64_t width, int r);
-int sb_lora_grad_a(const float* u32, const uint16_t* x, int64_t m, int64_t k, int r, float* da,
-                   void* workspace, size_t workspace_bytes, void* stream);
-int sb_lora_grad_b(const uint16_t* dy, const uint16_t* z, int64_t m, int64_t n, int r,
-                   float scale, float* db, void* workspace, size_t workspace_bytes,
-                   void* stream);
-/* at[k, r] = a[r, k] (fp16 transpose of lora_A for the dX epilogue term). */
-int sb_lora_transpose_a(const uint16_t* a, int r, int64_t k, uint16_t* at, void* stream);
+ * The low-rank products around the base projection: the PEFT lora_A / lora_B
+ * nn.Linear pair under fp16 autocast (solution/lora.py:161) and its autograd
+ * backward.  Rank r is 16, 32 or 64 (smaller ranks are zero-padded by the caller).
+ *
+ * sb_lora_prepare: lora_A [r, k] and lora_B [n, r] (fp16 or fp32) -> fp16 copies
+ *   a16 [r, k], at16 [k, r], b16 [n, r], bt16 [r, n] (any output may be NULL).
+ * sb_lora_project: P = X[m, k] . W[r, k]^T; writes fp16(scale_rows * P) row-major
+ *   with row pitch ld_rows, and/or fp16(scale_t * P)^T as [r, ldt] with rows
+ *   m..ldt-1 of the last 16-row tile zero-filled.  k % 32 == 0, 16-byte aligned
+ *   x and w.  Forward: Z = X.A^T (W = a16); backward: U = dY.B (W = bt16).
+ * sb_lora_reduce: out[r, w] = scale * Pt[r, ldp] . Q[ldp, w] over the first m rows
+ *   of Q (rows m..ldp-1 of Pt must be zero), out transposed to [w, r] when
+ *   transpose != 0, stored in out_dtype.  dA = U^T.X; dB = s * (Z^T.dY)^T.
+ *   Deterministic two-stage reduction through `workspace`
+ *   (sb_lora_reduce_workspace_bytes(m, w, r) bytes). */
+int sb_lora_prepare(const void* a, int a_dtype, const void* b, int b_dtype, int r, int64_t k,
+                    int64_t n, uint16_t* a16, uint16_t* at16, uint16_t* b16, uint16_t* bt16,
+                    void* stream);
+int sb_lora_project(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int r,
+                    float scale_rows, uint16_t* out_rows, int ld_rows, float scale_t,
+                    uint16_t* out_t, int64_t ldt, void* stream);
+size_t sb_lora_reduce_workspace_bytes(int64_t m, int64_t w, int r);
+int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m, int64_t w, int r,
+                   float scale, int transpose, void* out, int out_dtype, void* workspace,
+                   size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- LoRA epilogue
  * lora_scale_add_kernel / lora_scale_gradient_kernel

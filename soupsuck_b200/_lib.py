@@ -41,12 +41,10 @@ SIGNATURES = {
     "sb_nf4_linear_fwd": (_I32, [_P, _I64, ctypes.POINTER(NF4Weight), _P, _P, _P, _I32, _P, _P, _SZ, _P]),
     "sb_nf4_linear_dx": (_I32, [_P, _I64, ctypes.POINTER(NF4Weight), _P, _P, _I32, _P, _P, _SZ, _P]),
     "sb_nf4_linear_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
-    "sb_lora_down": (_I32, [_P, _I64, _I64, _P, _I32, _F32, _P, _P, _P]),
-    "sb_lora_up_grad": (_I32, [_P, _I64, _I64, _P, _I32, _F32, _P, _P, _P]),
-    "sb_lora_grad_workspace_bytes": (_SZ, [_I64, _I64, _I32]),
-    "sb_lora_grad_a": (_I32, [_P, _P, _I64, _I64, _I32, _P, _P, _SZ, _P]),
-    "sb_lora_grad_b": (_I32, [_P, _P, _I64, _I64, _I32, _F32, _P, _P, _SZ, _P]),
-    "sb_lora_transpose_a": (_I32, [_P, _I32, _I64, _P, _P]),
+    "sb_lora_prepare": (_I32, [_P, _I32, _P, _I32, _I32, _I64, _I64, _P, _P, _P, _P, _P]),
+    "sb_lora_project": (_I32, [_P, _I64, _I64, _P, _I32, _F32, _P, _I32, _F32, _P, _I64, _P]),
+    "sb_lora_reduce_workspace_bytes": (_SZ, [_I64, _I64, _I32]),
+    "sb_lora_reduce": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _F32, _I32, _P, _I32, _P, _SZ, _P]),
     "sb_lora_scale_add": (_I32, [_P, _I32, _P, _I32, _P, _I32, _I64, _F32, _I32, _P]),
     "sb_lora_scale_grad": (_I32, [_P, _I32, _P, _I32, _I64, _F32, _P]),
     "sb_add_rmsnorm_fwd": (_I32, [_P, _I32, _P, _I32, _P, _I32, _I64, _P, _P, _I32, _P, _I64, _I64, _F32, _P]),

@@ -98,10 +98,10 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
   if (rc) return rc;
   if (!dx) {
     rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.k_in / 2, w.n_out, w.k_in / 2, 32, kNF4BN,
-                  CU_TENSOR_MAP_SWIZZLE_NONE);
+                  CU_TENSOR_MAP_SWIZZLE_32B);
   } else {
     rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, w.k_in / 2, w.n_out, w.k_in / 2, kNF4BN / 2, 64,
-                  CU_TENSOR_MAP_SWIZZLE_NONE);
+                  CU_TENSOR_MAP_SWIZZLE_64B);
   }
   if (rc) return rc;
   tla = ta;

@@ -80,7 +80,7 @@ struct Cfg {
   static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
   static constexpr int kTmemCols = 2 * MSUB * BN;
   static constexpr int kThreads = kNF4 ? 512 : 256;
-  static constexpr int kBarrierBytes = 1024;
+  static constexpr int kBarrierBytes = 1024 + 1024;  // barriers + the 256-entry code2 table
   static constexpr int kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 1024;  // + align slack
   static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
   static_assert(BN % 64 == 0 && BN <= 256, "BN");
@@ -135,10 +135,10 @@ __device__ __forceinline__ void nf4_table(float scale, uint32_t (&L)[4], uint32_
   }
 }
 
-// Decode one 64-element block (32 packed bytes at `raw`) into a 128-byte
+// Decode one 64-element block (packed bytes 0-15 at `raw_lo`, 16-31 at `raw_hi`) into a 128-byte
 // swizzled SMEM row at `dst` (row index `r` inside its 8-row swizzle atom).
-__device__ __forceinline__ void nf4_decode_row(const uint8_t* raw, uint8_t* dst, int r,
-                                               float scale, bool valid) {
+__device__ __forceinline__ void nf4_decode_row(const uint8_t* raw_lo, const uint8_t* raw_hi,
+                                               uint8_t* dst, int r, float scale, bool valid) {
   const uint32_t swz = static_cast<uint32_t>(r & 7);
   if (!valid) {
 #pragma unroll
@@ -147,8 +147,8 @@ __device__ __forceinline__ void nf4_decode_row(const uint8_t* raw, uint8_t* dst,
     }
     return;
   }
-  const uint4 p0 = *reinterpret_cast<const uint4*>(raw);
-  const uint4 p1 = *reinterpret_cast<const uint4*>(raw + 16);
+  const uint4 p0 = *reinterpret_cast<const uint4*>(raw_lo);
+  const uint4 p1 = *reinterpret_cast<const uint4*>(raw_hi);
   uint32_t L[4], H[4];
   nf4_table(scale, L, H);
   const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
@@ -346,6 +346,7 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* code2_s = reinterpret_cast<float*>(bar_area + 1024);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -365,6 +366,9 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
+  }
+  if constexpr (C::kNF4) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) code2_s[i] = __ldg(p.code2 + i);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::kTmemCols);
@@ -522,6 +526,11 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
     }
   } else if (C::kNF4 && warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders
+    // Group g decodes the k-steps whose global index has parity g.  Each thread
+    // owns BN/128 (row, 64-block) tasks per step; the qabs byte and absmax2 value
+    // of its next step are loaded while the current one decodes, and code2 is
+    // read from shared memory, so no dependent global load sits on the critical path.
+    constexpr int kTasks = BN / 128;
     const int group = (warp - 8) >> 2;
     const int gtid = ((warp - 8) & 3) * 32 + lane;
     const float off = __ldg(p.offset);
@@ -529,34 +538,71 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
     const int rows_valid = runtime_rows(p);
     uint32_t it = 0;
     bool ok = true;
+    // Block index of task t at k-step `step` of the tile starting at output column n0,
+    // or -1 when that (row, block) lies outside the weight (written as zeros).
+    auto block_of = [&](int n0, int step, int task) -> int64_t {
+      if constexpr (BMODE == kNF4Fwd) {
+        const int64_t wrow = n0 + task;
+        return wrow < p.w_rows ? wrow * bpr + step : -1;
+      } else {
+        constexpr int kPanels = BN / 64;
+        const int64_t wrow = static_cast<int64_t>(step) * kBK + task / kPanels;
+        const int64_t wcol = n0 + 64 * (task % kPanels);
+        return (wrow < p.w_rows && wcol < p.w_cols) ? wrow * bpr + wcol / 64 : -1;
+      }
+    };
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       if ((tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
-      const int nt = tile / p.m_tiles;
-      const int n0 = nt * BN;
+      const int n0 = (tile / p.m_tiles) * BN;
+      // First step of this tile owned by this group.
+      int first = (static_cast<int>(it & 1) == group) ? 0 : 1;
+      uint32_t q_next[kTasks];
+      float a2_next[kTasks];
+#pragma unroll
+      for (int t = 0; t < kTasks; ++t) {
+        const int64_t blk = first < p.k_blocks ? block_of(n0, first, gtid + 128 * t) : -1;
+        q_next[t] = blk >= 0 ? __ldg(p.qabs + blk) : 0u;
+        a2_next[t] = blk >= 0 ? __ldg(p.absmax2 + (blk >> 8)) : 0.0f;
+      }
       for (int step = 0; step < steps; ++step, ++it) {
         if (static_cast<int>(it & 1) != group) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
+        uint32_t q_cur[kTasks];
+        float a2_cur[kTasks];
+        bool valid[kTasks];
+#pragma unroll
+        for (int t = 0; t < kTasks; ++t) {
+          q_cur[t] = q_next[t];
+          a2_cur[t] = a2_next[t];
+          valid[t] = step < p.k_blocks && block_of(n0, step, gtid + 128 * t) >= 0;
+          const int64_t nb = step + 2 < p.k_blocks ? block_of(n0, step + 2, gtid + 128 * t) : -1;
+          q_next[t] = nb >= 0 ? __ldg(p.qabs + nb) : 0u;
+          a2_next[t] = nb >= 0 ? __ldg(p.absmax2 + (nb >> 8)) : 0.0f;
+        }
         if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
         if (step < p.k_blocks) {
           uint8_t* b_s = smem + s * C::kStageBytes + C::kABytes;
           const uint8_t* raw_s = b_s + C::kBBytes;
 #pragma unroll
-          for (int task = gtid; task < BN; task += 128) {
+          for (int t = 0; t < kTasks; ++t) {
+            const int task = gtid + 128 * t;
+            const float scale = valid[t] ? __fadd_rn(__fmul_rn(code2_s[q_cur[t]], a2_cur[t]), off) : 0.0f;
             if constexpr (BMODE == kNF4Fwd) {
+              // Raw rows are 32 B, TMA-swizzled in 32 B spans: chunk ^= (row >> 2) & 1.
               const int r = task;
-              const int64_t wrow = n0 + r;
-              const bool valid = wrow < p.w_rows;
-              const float scale = valid ? nf4_scale(p, wrow * bpr + step, off) : 0.0f;
-              nf4_decode_row(raw_s + r * 32, b_s + r * 128, r, scale, valid);
+              const uint32_t x = static_cast<uint32_t>((r >> 2) & 1);
+              nf4_decode_row(raw_s + r * 32 + (x << 4), raw_s + r * 32 + ((x ^ 1u) << 4),
+                             b_s + r * 128, r, scale, valid[t]);
             } else {
+              // Raw rows are BN/2 = 64 B, TMA-swizzled in 64 B spans: chunk ^= (row >> 1) & 3.
               constexpr int kPanels = BN / 64;
+              static_assert(BMODE != kNF4Dx || BN == 128, "dX raw swizzle assumes 64-byte raw rows");
               const int r = task / kPanels, j = task % kPanels;
-              const int64_t wrow = static_cast<int64_t>(step) * kBK + r;
-              const int64_t wcol = n0 + 64 * j;
-              const bool valid = wrow < p.w_rows && wcol < p.w_cols;
-              const float scale = valid ? nf4_scale(p, wrow * bpr + wcol / 64, off) : 0.0f;
-              nf4_decode_row(raw_s + r * (BN / 2) + j * 32, b_s + j * (kBK * 128) + r * 128, r, scale, valid);
+              const uint32_t x = static_cast<uint32_t>((r >> 1) & 3);
+              const uint8_t* row = raw_s + r * 64;
+              nf4_decode_row(row + (((2u * j) ^ x) << 4), row + (((2u * j + 1u) ^ x) << 4),
+                             b_s + j * (kBK * 128) + r * 128, r, scale, valid[t]);
             }
           }
         }

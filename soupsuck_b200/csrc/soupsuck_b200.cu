@@ -6,4 +6,5 @@
 #include "gemm_sm100.cuh"
 #include "gemm_host.cuh"
 #include "linear.cuh"
+#include "lora_mma.cuh"
 #include "cross_entropy.cuh"

@@ -49,14 +49,6 @@ def _padded_rank(r):
     raise ValueError("LoRA rank above 64 is not supported")
 
 
-def _pad_cols(t, width):
-    if t.shape[-1] == width:
-        return t.contiguous()
-    out = torch.zeros((*t.shape[:-1], width), dtype=t.dtype, device=t.device)
-    out[..., :t.shape[-1]] = t
-    return out
-
-
 def nf4_linear_raw(x2d, packed, state, *, transpose=False, bias=None, lora_a=None, lora_b=None):
     """One launch of the fused GEMM.  lora_a [m, r] and lora_b [width, r] are the
     already-scaled fp16 low-rank factors (r padded to 16/32/64); no autograd."""
@@ -98,24 +90,57 @@ def nf4_matmul(x, packed, state, *, transpose=False, bias=None, config=None):
     return out.reshape(*x.shape[:-1], width)
 
 
-def _lora_factors_fwd(x2d, a16, b16, scaling):
-    """zs = fp16(s * X . A^T) [m, rp] and z = fp16(X . A^T) [m, r] (saved for dB)."""
+def _round16(m):
+    return (m + 15) // 16 * 16
+
+
+class _LoRAFactors:
+    """fp16 copies of the LoRA weights, zero-padded to a supported rank:
+    a16 [rp, K], at16 [K, rp], b16 [N, rp], bt16 [rp, N] (one sb_lora_prepare launch)."""
+
+    def __init__(self, lora_a, lora_b):
+        r, k = lora_a.shape
+        n = lora_b.shape[0]
+        rp = _padded_rank(r)
+        a, b = lora_a.detach(), lora_b.detach()
+        if rp != r:
+            a = torch.cat([a, a.new_zeros((rp - r, k))])
+            b = torch.cat([b, b.new_zeros((n, rp - r))], dim=1)
+        a, b = a.contiguous(), b.contiguous()
+        dev = a.device
+        self.r, self.rp = r, rp
+        self.a16 = torch.empty((rp, k), dtype=torch.float16, device=dev)
+        self.at16 = torch.empty((k, rp), dtype=torch.float16, device=dev)
+        self.b16 = torch.empty((n, rp), dtype=torch.float16, device=dev)
+        self.bt16 = torch.empty((rp, n), dtype=torch.float16, device=dev)
+        _lib.call("sb_lora_prepare", a.data_ptr(), _lib.dtype_code(a.dtype), b.data_ptr(),
+                  _lib.dtype_code(b.dtype), rp, k, n, self.a16.data_ptr(), self.at16.data_ptr(),
+                  self.b16.data_ptr(), self.bt16.data_ptr(), _lib.stream_of(dev))
+
+
+def _project(x2d, w16, rp, scale_rows, want_rows, scale_t, want_t):
+    """rows = fp16(scale_rows * X.W^T) [m, rp]; t = fp16(scale_t * X.W^T)^T [rp, m16]."""
     m, k = x2d.shape
-    r = a16.shape[0]
-    rp = _padded_rank(r)
-    z = torch.empty((m, r), dtype=torch.float16, device=x2d.device)
-    zs = torch.zeros((m, rp), dtype=torch.float16, device=x2d.device) if rp != r else \
-        torch.empty((m, r), dtype=torch.float16, device=x2d.device)
+    rows = torch.empty((m, rp), dtype=torch.float16, device=x2d.device) if want_rows else None
+    ldt = _round16(m)
+    tr = torch.empty((rp, ldt), dtype=torch.float16, device=x2d.device) if want_t else None
     if m:
-        if rp == r:
-            _lib.call("sb_lora_down", x2d.data_ptr(), m, k, a16.data_ptr(), r, float(scaling),
-                      z.data_ptr(), zs.data_ptr(), _lib.stream_of(x2d.device))
-        else:
-            tmp = torch.empty((m, r), dtype=torch.float16, device=x2d.device)
-            _lib.call("sb_lora_down", x2d.data_ptr(), m, k, a16.data_ptr(), r, float(scaling),
-                      z.data_ptr(), tmp.data_ptr(), _lib.stream_of(x2d.device))
-            zs[:, :r] = tmp
-    return z, zs, rp
+        _lib.call("sb_lora_project", x2d.data_ptr(), m, k, w16.data_ptr(), rp, float(scale_rows),
+                  _lib.ptr(rows), rp, float(scale_t), _lib.ptr(tr), ldt, _lib.stream_of(x2d.device))
+    return rows, tr
+
+
+def _reduce(pt, q2d, rp, scale, transpose, out_dtype):
+    """scale * (pt[:, :m] . q)  -> [rp, w] (or [w, rp] when transposed) in out_dtype."""
+    m, w = q2d.shape
+    shape = (w, rp) if transpose else (rp, w)
+    out = torch.empty(shape, dtype=out_dtype, device=q2d.device)
+    nbytes = _lib.query("sb_lora_reduce_workspace_bytes", m, w, rp)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q2d.device)
+    _lib.call("sb_lora_reduce", _lib.ptr(pt), pt.shape[1] if pt is not None else _round16(m),
+              q2d.data_ptr(), m, w, rp, float(scale), int(transpose), out.data_ptr(),
+              _lib.dtype_code(out_dtype), ws.data_ptr(), nbytes, _lib.stream_of(q2d.device))
+    return out
 
 
 class _NF4LoRALinear(torch.autograd.Function):
@@ -126,60 +151,45 @@ class _NF4LoRALinear(torch.autograd.Function):
         if not x2d.is_contiguous():
             x2d = x2d.contiguous()
         has_lora = lora_a is not None
-        z = None
+        f = zt = None
         if has_lora:
-            a16 = lora_a.detach().to(torch.float16).contiguous()
-            b16 = lora_b.detach().to(torch.float16).contiguous()
-            z, zs, rp = _lora_factors_fwd(x2d, a16, b16, scaling)
-            y = nf4_linear_raw(x2d, packed, state, bias=bias, lora_a=zs, lora_b=_pad_cols(b16, rp))
+            f = _LoRAFactors(lora_a, lora_b)
+            zs, zt = _project(x2d, f.a16, f.rp, scaling, True, 1.0, True)
+            y = nf4_linear_raw(x2d, packed, state, bias=bias, lora_a=zs, lora_b=f.b16)
+            ctx.a_dtype, ctx.b_dtype = lora_a.dtype, lora_b.dtype
+            ctx.save_for_backward(x2d, packed, zt, f.at16, f.bt16)
         else:
             y = nf4_linear_raw(x2d, packed, state, bias=bias)
-        ctx.save_for_backward(x2d, packed, z, lora_a, lora_b)
+            ctx.save_for_backward(x2d, packed)
         ctx.state, ctx.scaling, ctx.has_lora = state, float(scaling), has_lora
+        ctx.r = f.r if has_lora else 0
         ctx.x_shape = x.shape
         return y.reshape(*x.shape[:-1], n)
 
     @staticmethod
     @once_differentiable
     def backward(ctx, grad):
-        x2d, packed, z, lora_a, lora_b = ctx.saved_tensors
         state = ctx.state
         n, k = state.shape
-        g = grad.reshape(-1, n).to(torch.float16).contiguous()
-        m = g.shape[0]
+        g = grad.reshape(-1, n)
+        if g.dtype != torch.float16 or not g.is_contiguous():
+            g = g.to(torch.float16).contiguous()
         dx = da = db = None
-        stream = _lib.stream_of(g.device)
         if ctx.has_lora:
-            r = lora_a.shape[0]
-            rp = _padded_rank(r)
-            b16 = lora_b.detach().to(torch.float16).contiguous()
-            a16 = lora_a.detach().to(torch.float16).contiguous()
-            u32 = torch.empty((m, r), dtype=torch.float32, device=g.device)
-            u16 = torch.empty((m, r), dtype=torch.float16, device=g.device)
-            if m:
-                _lib.call("sb_lora_up_grad", g.data_ptr(), m, n, b16.data_ptr(), r, ctx.scaling,
-                          u16.data_ptr(), u32.data_ptr(), stream)
-            at = torch.empty((k, r), dtype=torch.float16, device=g.device)
-            _lib.call("sb_lora_transpose_a", a16.data_ptr(), r, k, at.data_ptr(), stream)
+            x2d, packed, zt, at16, bt16 = ctx.saved_tensors
+            rp, r, s = at16.shape[1], ctx.r, ctx.scaling
+            need_x, need_a, need_b = ctx.needs_input_grad[0], ctx.needs_input_grad[3], ctx.needs_input_grad[4]
+            u, ut = _project(g, bt16, rp, s, need_x, s, need_a)
+            if need_x:
+                dx = nf4_linear_raw(g, packed, state, transpose=True, lora_a=u, lora_b=at16)
+            if need_a:
+                da = _reduce(ut, x2d, rp, 1.0, False, ctx.a_dtype)[:r]
+            if need_b:
+                db = _reduce(zt, g, rp, s, True, ctx.b_dtype)[:, :r]
+        else:
+            x2d, packed = ctx.saved_tensors
             if ctx.needs_input_grad[0]:
-                dx = nf4_linear_raw(g, packed, state, transpose=True,
-                                    lora_a=_pad_cols(u16, rp), lora_b=_pad_cols(at, rp))
-            if ctx.needs_input_grad[3]:
-                da = torch.empty((r, k), dtype=torch.float32, device=g.device)
-                nb = _lib.query("sb_lora_grad_workspace_bytes", m, k, r)
-                ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=g.device)
-                _lib.call("sb_lora_grad_a", u32.data_ptr(), x2d.data_ptr(), m, k, r, da.data_ptr(),
-                          ws.data_ptr(), nb, stream)
-                da = da.to(lora_a.dtype)
-            if ctx.needs_input_grad[4]:
-                db = torch.empty((n, r), dtype=torch.float32, device=g.device)
-                nb = _lib.query("sb_lora_grad_workspace_bytes", m, n, r)
-                ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=g.device)
-                _lib.call("sb_lora_grad_b", g.data_ptr(), z.data_ptr(), m, n, r, ctx.scaling,
-                          db.data_ptr(), ws.data_ptr(), nb, stream)
-                db = db.to(lora_b.dtype)
-        elif ctx.needs_input_grad[0]:
-            dx = nf4_linear_raw(g, packed, state, transpose=True)
+                dx = nf4_linear_raw(g, packed, state, transpose=True)
         if dx is not None:
             dx = dx.reshape(ctx.x_shape)
         return dx, None, None, da, db, None, None
@@ -203,6 +213,10 @@ def nf4_lora_linear(x, packed, state, lora_a=None, lora_b=None, scaling=1.0, bia
                 or lora_a.shape[0] != lora_b.shape[1] or lora_a.device != x.device
                 or lora_b.device != x.device):
             raise ValueError("Expected lora_a[r, K] and lora_b[N, r] on the input's device")
+        if lora_a.dtype not in (torch.float16, torch.float32) or lora_b.dtype not in (torch.float16, torch.float32):
+            raise ValueError("LoRA weights must be fp16 or fp32")
+        if k % 32 or n % 32:
+            raise ValueError("The fused LoRA path needs K and N multiples of 32")
         _padded_rank(lora_a.shape[0])
     if bias is not None and (bias.dtype != torch.float16 or bias.shape != (n,) or bias.requires_grad
                              or bias.device != x.device):
