@@ -92,7 +92,10 @@ int sb_nf4_linear_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight* w,
                      const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* dx,
                      void* workspace, size_t workspace_bytes, void* stream);
 
-/* Scratch bytes the two calls above need for these sizes (0 on the tcgen05 path). */
+/* Scratch bytes the two calls above need for these sizes, assuming 16-byte aligned
+ * x/dy, packed and LoRA pointers: fp32 partial tiles and per-tile counters when the
+ * tcgen05 path splits tiles across CTAs (stream-K), or the decoded weight when an
+ * odd shape takes the CUDA-core path. */
 size_t sb_nf4_linear_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in, int dx);
 
 /* ---------------------------------------------------------------- LoRA factors

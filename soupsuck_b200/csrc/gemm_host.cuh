@@ -2,7 +2,9 @@
 // NF4-linear / cross-entropy drivers exported through the C ABI.
 #pragma once
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "gemm_sm100.cuh"
@@ -51,6 +53,47 @@ inline CUtensorMapSwizzle lora_swizzle(int r) {
   return r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : (r == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Schedule override from the environment: SB_STREAMK=0 (whole tiles), 1 (stream-K)
+// or unset / "auto" (the heuristic below).  Read once per process.
+inline int streamk_override() {
+  static int v = [] {
+    const char* e = std::getenv("SB_STREAMK");
+    if (!e || !*e || std::string(e) == "auto") return -1;
+    return std::string(e) == "0" ? 0 : 1;
+  }();
+  return v;
+}
+
+// Stream-K pays off when whole tiles would leave the last wave mostly idle and a
+// tile is long enough (>= 64 k-blocks) to amortise the partial-tile write and
+// fix-up; measured on B200, short reductions (24 k-blocks) lose more to the
+// fix-up traffic than they gain from balance.
+inline bool want_streamk(int64_t tiles, int64_t k_blocks, int sms) {
+  if (tiles <= 0 || k_blocks < 4) return false;
+  if (streamk_override() >= 0) return streamk_override() == 1;
+  if (k_blocks < 64) return false;
+  const int64_t waves = (tiles + sms - 1) / sms;
+  return static_cast<double>(tiles) / static_cast<double>(waves * sms) < 0.9;
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Stream-K grid: every CTA gets at least half a tile of k-iterations, so a tile is
+// shared by at most about two CTAs and the fix-up stays cheap.
+inline int streamk_grid(int64_t tiles, int64_t k_blocks, int sms) {
+  int64_t g = 2 * tiles;
+  if (g > sms) g = sms;
+  const int64_t total = tiles * k_blocks;
+  if (g > total) g = total;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+// Scratch of a stream-K launch: two fp32 partial tiles per CTA, then one counter per tile.
+inline size_t streamk_bytes(int grid, int tile_rows, int tile_cols, int64_t tiles) {
+  return align256(static_cast<size_t>(grid) * 2 * tile_rows * tile_cols * sizeof(float)) +
+         align256(static_cast<size_t>(tiles) * sizeof(int));
+}
+
 template <int BMODE, int EMODE, int MSUB, int BN, int STAGES>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
            const CUtensorMap& lb, Params p, cudaStream_t stream, const char* name) {
@@ -71,7 +114,8 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
   const int tiles = p.m_tiles * p.n_tiles;
   if (tiles == 0) return SB_OK;
   const int sms = device_sm_count();
-  const int grid = tiles < sms ? tiles : sms;
+  int grid = tiles < sms ? tiles : sms;
+  if (p.streamk) grid = streamk_grid(tiles, p.k_blocks, sms);
   kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(a, b, la, lb, p);
   count_launch();
   return check_launch(name);
@@ -88,9 +132,33 @@ inline bool nf4_tc_shape_ok(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
   return true;
 }
 
+struct NF4Plan {
+  int64_t m_tiles, n_tiles, k_blocks;
+  bool streamk;
+  size_t workspace;
+};
+
+inline NF4Plan nf4_plan(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
+  NF4Plan pl{};
+  const int64_t red = dx ? n_out : k_in, width = dx ? k_in : n_out;
+  pl.m_tiles = (m + kNF4Msub * 128 - 1) / (kNF4Msub * 128);
+  pl.n_tiles = (width + kNF4BN - 1) / kNF4BN;
+  pl.k_blocks = (red + 63) / 64;
+  const int sms = device_sm_count();
+  pl.streamk = want_streamk(pl.m_tiles * pl.n_tiles, pl.k_blocks, sms);
+  pl.workspace = pl.streamk ? streamk_bytes(streamk_grid(pl.m_tiles * pl.n_tiles, pl.k_blocks, sms),
+                                            kNF4Msub * 128, kNF4BN, pl.m_tiles * pl.n_tiles) : 0;
+  return pl;
+}
+
 inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weight& w,
                          const uint16_t* bias, const uint16_t* lora_a, const uint16_t* lora_b,
-                         int r, uint16_t* out, cudaStream_t stream) {
+                         int r, uint16_t* out, void* workspace, size_t workspace_bytes,
+                         cudaStream_t stream) {
+  const NF4Plan pl = nf4_plan(m, w.n_out, w.k_in, dx);
+  if (pl.workspace > 0 && (!workspace || workspace_bytes < pl.workspace)) {
+    return fail(SB_EWORKSPACE, "NF4 linear needs " + std::to_string(pl.workspace) + " workspace bytes");
+  }
   const int64_t red = dx ? w.n_out : w.k_in;    // reduction length
   const int64_t width = dx ? w.k_in : w.n_out;  // output columns
   CUtensorMap ta, tb, tla, tlb;
@@ -116,10 +184,20 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
   p.M = static_cast<int>(m);
   p.N = static_cast<int>(width);
   p.K = static_cast<int>(red);
-  p.m_tiles = static_cast<int>((m + kNF4Msub * 128 - 1) / (kNF4Msub * 128));
-  p.n_tiles = static_cast<int>((width + kNF4BN - 1) / kNF4BN);
-  p.k_blocks = static_cast<int>((red + 63) / 64);
+  p.m_tiles = static_cast<int>(pl.m_tiles);
+  p.n_tiles = static_cast<int>(pl.n_tiles);
+  p.k_blocks = static_cast<int>(pl.k_blocks);
   p.lora_r = r;
+  if (pl.streamk) {
+    const int sms = device_sm_count();
+    p.streamk = 1;
+    p.partials = static_cast<float*>(workspace);
+    const int grid = streamk_grid(pl.m_tiles * pl.n_tiles, pl.k_blocks, sms);
+    p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
+                                        align256(static_cast<size_t>(grid) * 2 * kNF4Msub * 128 * kNF4BN * sizeof(float)));
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(pl.m_tiles * pl.n_tiles) * sizeof(int), stream);
+    if (e != cudaSuccess) return fail(SB_ECUDA, std::string("counter reset: ") + cudaGetErrorString(e));
+  }
   p.vec_ok = aligned(out, 16) && (width % 8 == 0);
   p.qabs = w.qabs;
   p.absmax2 = w.absmax2;

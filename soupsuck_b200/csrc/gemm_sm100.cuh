@@ -47,6 +47,9 @@ struct Params {
   int lora_r;             // 0, 16, 32 or 64: extra LoRA step(s) after the main loop
   const int* m_dev;       // optional runtime row count (CE backward compaction)
   int vec_ok;             // output rows are 16-byte aligned
+  int streamk;            // 1: stream-K schedule (equal k-iteration shares per CTA)
+  float* partials;        // stream-K: [grid, 2, MSUB*128, BN] fp32 partial tiles
+  int* counters;          // stream-K: [tiles] arrival counters, zero before launch
   // NF4 weight
   const uint8_t* qabs;
   const float* absmax2;
@@ -328,6 +331,69 @@ __device__ __forceinline__ void epilogue_end(const Params& p, const EpiState& st
   }
 }
 
+// ------------------------------------------------------------ work schedule
+// A work unit is one output tile over the k-blocks [k0, k1).  Tile mode: CTA c
+// takes tiles c, c + grid, ... whole.  Stream-K mode: the tile-major k-iteration
+// space T = tiles * k_blocks is cut into `grid` equal contiguous ranges, one per
+// CTA, so every SM gets the same amount of MMA work whatever the tile count; a
+// tile split between CTAs is finished by whichever contributor arrives last.
+struct Unit {
+  int tile, k0, k1;
+};
+
+struct UnitIter {
+  int64_t cursor, end;
+  int kb, stride;
+  bool streamk;
+  __device__ UnitIter(const Params& p, int num_tiles) {
+    streamk = p.streamk != 0;
+    kb = p.k_blocks;
+    if (streamk) {
+      const int64_t total = static_cast<int64_t>(num_tiles) * kb;
+      cursor = total * blockIdx.x / gridDim.x;
+      end = total * (blockIdx.x + 1) / gridDim.x;
+      stride = 0;
+    } else {
+      cursor = blockIdx.x;
+      end = num_tiles;
+      stride = gridDim.x;
+    }
+  }
+  __device__ bool next(Unit& u) {
+    if (cursor >= end) return false;
+    if (streamk) {
+      u.tile = static_cast<int>(cursor / kb);
+      u.k0 = static_cast<int>(cursor % kb);
+      const int64_t k1 = u.k0 + (end - cursor);
+      u.k1 = static_cast<int>(k1 < kb ? k1 : kb);
+      cursor += u.k1 - u.k0;
+    } else {
+      u.tile = static_cast<int>(cursor);
+      u.k0 = 0;
+      u.k1 = kb;
+      cursor += stride;
+    }
+    return true;
+  }
+};
+
+// Stream-K: the CTA whose iteration range contains iteration x.
+__device__ __forceinline__ int sk_owner(int64_t x, int64_t total, int grid) {
+  int c = static_cast<int>(x * grid / total);
+  while (c + 1 < grid && total * (c + 1) / grid <= x) ++c;
+  while (c > 0 && total * c / grid > x) --c;
+  return c;
+}
+
+// Bounded rendezvous of the 128 epilogue threads on an mbarrier (no unbounded bar.sync:
+// if a wait elsewhere gave up, the others leave after the time limit instead of hanging).
+__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, volatile int* abort) {
+  mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase, kErrWaitAccFull, abort);
+  phase ^= 1u;
+  return ok;
+}
+
 // ------------------------------------------------------------ the kernel
 template <int BMODE, int EMODE, int MSUB, int BN, int STAGES>
 __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
@@ -344,14 +410,16 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
   uint64_t* acc_full = decoded + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* epi_mb = drain + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(epi_mb + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* last_flag = abort_flag + 1;
   float* code2_s = reinterpret_cast<float*>(bar_area + 1024);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = p.m_tiles * p.n_tiles;
-  const int steps = p.k_blocks + (p.lora_r > 0 ? 1 : 0);
+  const bool has_lora = p.lora_r > 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -364,7 +432,9 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
       mbar_init(&acc_empty[b], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(epi_mb, 128);
     *abort_flag = 0;
+    *last_flag = 0;
     fence_barrier_init();
   }
   if constexpr (C::kNF4) {
@@ -377,31 +447,35 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const int rows_valid = runtime_rows(p);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      if (p.lora_r > 0) {
+      if (has_lora) {
         tma_prefetch_desc(&tmLA);
         tma_prefetch_desc(&tmLB);
       }
-      const int rows_valid = runtime_rows(p);
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+      UnitIter iter(p, num_tiles);
+      Unit u;
+      while (ok && iter.next(u)) {
+        const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
         const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
         if (m0 >= rows_valid) continue;
-        for (int step = 0; step < steps; ++step, ++it) {
+        const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
+        for (int ls = 0; ls < nsteps; ++ls, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) { ok = false; break; }
           uint8_t* a_s = smem + s * C::kStageBytes;
           uint8_t* b_s = a_s + C::kABytes;
           uint8_t* raw_s = b_s + C::kBBytes;
-          if (step < p.k_blocks) {
+          const int step = u.k0 + ls;
+          if (step < u.k1) {
             mbar_arrive_expect_tx(&full[s], C::kABytes + (C::kNF4 ? C::kRawBytes : C::kBBytes));
 #pragma unroll
             for (int ms = 0; ms < MSUB; ++ms) {
@@ -440,27 +514,30 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
       constexpr uint32_t kIdescLora = idesc_f16_f32(kTileRows, BN, 0, 0);
       const uint32_t lora_layout = p.lora_r == 16 ? kSwizzle32B : (p.lora_r == 32 ? kSwizzle64B : kSwizzle128B);
       const uint32_t lora_pitch = static_cast<uint32_t>(p.lora_r) * 2;
-      const int rows_valid = runtime_rows(p);
       uint32_t it = 0, tl = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if ((tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
+      UnitIter iter(p, num_tiles);
+      Unit u;
+      while (ok && iter.next(u)) {
+        if ((u.tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
         const int buf = tl & 1;
         const uint32_t aph = (tl >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * MSUB * BN;
-        for (int step = 0; step < steps; ++step, ++it) {
+        const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
+        for (int ls = 0; ls < nsteps; ++ls, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          const bool main_step = u.k0 + ls < u.k1;
           if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
-          if (C::kNF4 && step < p.k_blocks) {
+          if (C::kNF4 && main_step) {
             if (!mbar_wait(&decoded[s], ph, kErrWaitDecoded, abort_flag)) { ok = false; break; }
           }
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + s * C::kStageBytes);
           const uint32_t b_addr = a_addr + C::kABytes;
-          if (step < p.k_blocks) {
+          if (main_step) {
 #pragma unroll
             for (int k16 = 0; k16 < kBK / 16; ++k16) {
               const uint64_t bdesc = C::kBMN
@@ -469,7 +546,7 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
 #pragma unroll
               for (int ms = 0; ms < MSUB; ++ms) {
                 const uint64_t adesc = smem_desc(a_addr + ms * kTileRows * kBK * 2 + k16 * 32, 16, 1024, kSwizzle128B);
-                umma_f16(acc + ms * BN, adesc, bdesc, kIdesc, (step > 0 || k16 > 0) ? 1u : 0u);
+                umma_f16(acc + ms * BN, adesc, bdesc, kIdesc, (ls > 0 || k16 > 0) ? 1u : 0u);
               }
             }
           } else {
@@ -496,33 +573,130 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int rows_valid = runtime_rows(p);
-    uint32_t tl = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+    const int etid = (warp - 4) * 32 + lane;
+    const int64_t total = static_cast<int64_t>(num_tiles) * p.k_blocks;
+    uint32_t tl = 0, epi_phase = 0;
+    int uidx = 0;
+    UnitIter iter(p, num_tiles);
+    Unit u;
+    while (iter.next(u)) {
+      const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
       const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
       if (m0 >= rows_valid) continue;
       const int buf = tl & 1;
       const uint32_t aph = (tl >> 1) & 1;
       if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) break;
       tc_fence_after();
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * MSUB * BN;
+      if (u.k0 == 0 && u.k1 == p.k_blocks) {
 #pragma unroll 1
-      for (int ms = 0; ms < MSUB; ++ms) {
-        const int row = m0 + ms * kTileRows + q * 32 + lane;
-        EpiState st;
-        epilogue_begin<EMODE>(p, st, row, rows_valid);
+        for (int ms = 0; ms < MSUB; ++ms) {
+          const int row = m0 + ms * kTileRows + q * 32 + lane;
+          EpiState st;
+          epilogue_begin<EMODE>(p, st, row, rows_valid);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * MSUB * BN + ms * BN + c * 32, v);
-          tmem_ld_wait();
-          epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tacc + ms * BN + c * 32, v);
+            tmem_ld_wait();
+            epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+          }
+          epilogue_end<EMODE>(p, st, row, nt, rows_valid);
         }
-        epilogue_end<EMODE>(p, st, row, nt, rows_valid);
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+      } else {
+        // Stream-K partial tile: park the fp32 accumulator in this CTA's slot,
+        // release TMEM, then let the last contributor to arrive sum every slot
+        // in CTA order (deterministic) and run the epilogue.
+        const int slot = uidx == 0 ? 0 : 1;
+        // Slot layout is thread-major ([ms][chunk][j][etid] float4) so each warp
+        // writes and later reads 512 contiguous bytes per instruction.
+        constexpr int kSlotF4 = MSUB * (BN / 32) * 8 * 128;  // float4 per slot
+        float4* mine = reinterpret_cast<float4*>(p.partials) + (static_cast<int64_t>(blockIdx.x) * 2 + slot) * kSlotF4;
+#pragma unroll 1
+        for (int ms = 0; ms < MSUB; ++ms) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tacc + ms * BN + c * 32, v);
+            tmem_ld_wait();
+            float4* dst = mine + ((ms * (BN / 32) + c) * 8) * 128 + etid;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              __stcg(dst + j * 128, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        __threadfence();
+        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+        const int64_t it0 = static_cast<int64_t>(u.tile) * p.k_blocks;
+        const int c_lo = sk_owner(it0, total, gridDim.x);
+        const int c_hi = sk_owner(it0 + p.k_blocks - 1, total, gridDim.x);
+        if (etid == 0) {
+          const int prev = atomicAdd(p.counters + u.tile, 1);
+          *last_flag = (prev == c_hi - c_lo) ? 1 : 0;
+        }
+        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+        const bool last = *last_flag != 0;
+        // Every thread has read the flag before it can be rewritten.
+        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+        if (last) {
+          __threadfence();
+#pragma unroll 1
+          for (int ms = 0; ms < MSUB; ++ms) {
+            const int lrow = ms * kTileRows + q * 32 + lane;
+            const int row = m0 + lrow;
+            EpiState st;
+            epilogue_begin<EMODE>(p, st, row, rows_valid);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              float sum[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+              const int64_t off = static_cast<int64_t>((ms * (BN / 32) + c) * 8) * 128 + etid;
+              // Contributors are summed in CTA order; their loads are issued
+              // in batches of four so the L2 round trips overlap.
+              for (int cc = c_lo; cc <= c_hi; cc += 4) {
+                float4 x[4][8];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                  const int ci = cc + b;
+                  if (ci <= c_hi) {
+                    const int64_t first_tile = (total * ci / gridDim.x) / p.k_blocks;
+                    const int cslot = first_tile == u.tile ? 0 : 1;
+                    const float4* src = reinterpret_cast<const float4*>(p.partials) +
+                                        (static_cast<int64_t>(ci) * 2 + cslot) * kSlotF4 + off;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) x[b][j] = __ldcg(src + j * 128);
+                  }
+                }
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                  if (cc + b <= c_hi) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                      sum[4 * j] += x[b][j].x; sum[4 * j + 1] += x[b][j].y;
+                      sum[4 * j + 2] += x[b][j].z; sum[4 * j + 3] += x[b][j].w;
+                    }
+                  }
+                }
+              }
+              uint32_t v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(sum[j]);
+              epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+            }
+            epilogue_end<EMODE>(p, st, row, nt, rows_valid);
+          }
+          if (etid == 0) p.counters[u.tile] = 0;  // ready for the next launch
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
       ++tl;
+      ++uidx;
     }
   } else if (C::kNF4 && warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders
@@ -535,7 +709,6 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
     const int gtid = ((warp - 8) & 3) * 32 + lane;
     const float off = __ldg(p.offset);
     const int64_t bpr = p.w_cols / 64;
-    const int rows_valid = runtime_rows(p);
     uint32_t it = 0;
     bool ok = true;
     // Block index of task t at k-step `step` of the tile starting at output column n0,
@@ -551,23 +724,28 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
         return (wrow < p.w_rows && wcol < p.w_cols) ? wrow * bpr + wcol / 64 : -1;
       }
     };
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      if ((tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
-      const int n0 = (tile / p.m_tiles) * BN;
-      // First step of this tile owned by this group.
-      int first = (static_cast<int>(it & 1) == group) ? 0 : 1;
+    UnitIter iter(p, num_tiles);
+    Unit u;
+    while (ok && iter.next(u)) {
+      if ((u.tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
+      const int n0 = (u.tile / p.m_tiles) * BN;
+      const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
+      // First k-step of this unit owned by this group.
+      const int first = u.k0 + ((static_cast<int>(it & 1) == group) ? 0 : 1);
       uint32_t q_next[kTasks];
       float a2_next[kTasks];
 #pragma unroll
       for (int t = 0; t < kTasks; ++t) {
-        const int64_t blk = first < p.k_blocks ? block_of(n0, first, gtid + 128 * t) : -1;
+        const int64_t blk = first < u.k1 ? block_of(n0, first, gtid + 128 * t) : -1;
         q_next[t] = blk >= 0 ? __ldg(p.qabs + blk) : 0u;
         a2_next[t] = blk >= 0 ? __ldg(p.absmax2 + (blk >> 8)) : 0.0f;
       }
-      for (int step = 0; step < steps; ++step, ++it) {
+      for (int ls = 0; ls < nsteps; ++ls, ++it) {
         if (static_cast<int>(it & 1) != group) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
+        const int step = u.k0 + ls;
+        const bool main_step = step < u.k1;
         uint32_t q_cur[kTasks];
         float a2_cur[kTasks];
         bool valid[kTasks];
@@ -575,13 +753,13 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
         for (int t = 0; t < kTasks; ++t) {
           q_cur[t] = q_next[t];
           a2_cur[t] = a2_next[t];
-          valid[t] = step < p.k_blocks && block_of(n0, step, gtid + 128 * t) >= 0;
-          const int64_t nb = step + 2 < p.k_blocks ? block_of(n0, step + 2, gtid + 128 * t) : -1;
+          valid[t] = main_step && block_of(n0, step, gtid + 128 * t) >= 0;
+          const int64_t nb = step + 2 < u.k1 ? block_of(n0, step + 2, gtid + 128 * t) : -1;
           q_next[t] = nb >= 0 ? __ldg(p.qabs + nb) : 0u;
           a2_next[t] = nb >= 0 ? __ldg(p.absmax2 + (nb >> 8)) : 0.0f;
         }
         if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
-        if (step < p.k_blocks) {
+        if (main_step) {
           uint8_t* b_s = smem + s * C::kStageBytes + C::kABytes;
           const uint8_t* raw_s = b_s + C::kBBytes;
 #pragma unroll

@@ -103,7 +103,8 @@ inline int nf4_linear(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weig
   const bool ptrs_ok = aligned(act, 16) && aligned(w->packed, 16) &&
                        (r == 0 || (aligned(lora_a, 16) && aligned(lora_b, 16)));
   if (tc_rank && ptrs_ok && gemm::nf4_tc_shape_ok(m, w->n_out, w->k_in, dx)) {
-    return gemm::nf4_linear_tc(dx, act, m, *w, bias, lora_a, lora_b, r, out, st);
+    return gemm::nf4_linear_tc(dx, act, m, *w, bias, lora_a, lora_b, r, out, workspace,
+                               workspace_bytes, st);
   }
   return nf4_linear_fallback(dx, act, m, *w, bias, lora_a, lora_b, r, out, workspace,
                              workspace_bytes, st);
@@ -115,8 +116,10 @@ extern "C" {
 
 size_t sb_nf4_linear_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in, int dx) {
   if (m <= 0 || n_out <= 0 || k_in <= 0) return 0;
-  if (sb::gemm::nf4_tc_shape_ok(m, n_out, k_in, dx != 0)) return 0;
-  return static_cast<size_t>(n_out) * k_in * 2;
+  // Shapes the tcgen05 path takes (with 16-byte aligned operands, which the
+  // caller guarantees) need only its stream-K scratch; others the decoded weight.
+  if (!sb::gemm::nf4_tc_shape_ok(m, n_out, k_in, dx != 0)) return static_cast<size_t>(n_out) * k_in * 2;
+  return sb::gemm::nf4_plan(m, n_out, k_in, dx != 0).workspace;
 }
 
 int sb_nf4_linear_fwd(const uint16_t* x, int64_t m, const sb_nf4_weight* w, const uint16_t* bias,

@@ -49,11 +49,19 @@ def _padded_rank(r):
     raise ValueError("LoRA rank above 64 is not supported")
 
 
+def _aligned16(t):
+    """The kernels take 16-byte aligned operands; copy the rare misaligned view."""
+    if t is None or t.data_ptr() % 16 == 0:
+        return t
+    return t.clone()
+
+
 def nf4_linear_raw(x2d, packed, state, *, transpose=False, bias=None, lora_a=None, lora_b=None):
     """One launch of the fused GEMM.  lora_a [m, r] and lora_b [width, r] are the
     already-scaled fp16 low-rank factors (r padded to 16/32/64); no autograd."""
     n, k = state.shape
     m = x2d.shape[0]
+    x2d, packed, lora_a, lora_b = (_aligned16(t) for t in (x2d, packed, lora_a, lora_b))
     width = k if transpose else n
     out = torch.empty((m, width), dtype=torch.float16, device=x2d.device)
     if m == 0:
