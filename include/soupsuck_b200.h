@@ -124,6 +124,18 @@ size_t sb_lora_reduce_workspace_bytes(int64_t m, int64_t w, int r);
 int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m, int64_t w, int r,
                    float scale, int transpose, void* out, int out_dtype, void* workspace,
                    size_t workspace_bytes, void* stream);
+/* sb_lora_reduce without any allocation or workspace, for callers that cannot
+ * allocate device memory (memory planned once at start-up, foreign-language
+ * bindings without a CUDA allocator, steps that must not grow their footprint).
+ * No counterpart in the reference: its reduction always allocates through the
+ * PyTorch caching allocator.  The fp32 partial sums live in one fixed 8 MiB
+ * device array inside this library (kept by every GPU that loads it until the
+ * process exits); r * w above 2,097,152 is rejected with SB_EINVAL.  All calls
+ * share that array and calls that overlap on the GPU race on it; nothing in it
+ * has to start at zero.  The first call on a device looks up the array with
+ * that device current: make it before any stream capture. */
+int sb_lora_reduce_static(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m, int64_t w,
+                          int r, float scale, int transpose, void* out, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------- LoRA epilogue
  * lora_scale_add_kernel / lora_scale_gradient_kernel

@@ -7,4 +7,5 @@
 #include "gemm_host.cuh"
 #include "linear.cuh"
 #include "lora_mma.cuh"
+#include "lora_static.cuh"
 #include "cross_entropy.cuh"

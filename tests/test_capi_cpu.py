@@ -54,6 +54,7 @@ def test_invalid_arguments_fail_before_any_launch(lib):
     assert lib.sb_nf4_dequant_nested(None, None, None, None, None, None, -1, None) == _lib.SB_EINVAL
     assert b"non-negative" in lib.sb_last_error()
     assert lib.sb_lora_project(None, 10, 33, None, 16, 1.0, None, 16, 1.0, None, 16, None) == _lib.SB_EINVAL
+    assert lib.sb_lora_reduce_static(None, 16, None, 16, 65536, 64, 1.0, 0, ctypes.c_void_p(1), 1, None) == _lib.SB_EINVAL
     assert lib.sb_launch_count() == before
 
 
