@@ -210,7 +210,7 @@ def run_reference(args, torch):
 
 
 # ------------------------------------------------------------------ GPU timing helpers
-def gemm_roofline(torch, layer, device, t):
+def gemm_roofline(torch, layer, device, t, passes=10, warm=3):
     """Time the fused NF4 GEMM launches of one step (forward and dX of all seven
     projections, LoRA fused) back to back with CUDA events on their stream."""
     from soupsuck_b200.kernels.nf4_gemm import nf4_linear_raw
@@ -228,13 +228,13 @@ def gemm_roofline(torch, layer, device, t):
         f, d = proj_flops(t, n, k, RANK_R)
         flops += f + d
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
-    for _ in range(3):
+    for _ in range(warm):
         for c in calls:
             c()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(device)
     times = []
-    for _ in range(10):
+    for _ in range(passes):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -247,9 +247,9 @@ def gemm_roofline(torch, layer, device, t):
     return flops, sec, len(calls)
 
 
-def ce_benchmark(torch, device, steps):
+def ce_benchmark(torch, device, steps, tokens=T_TOKENS, warm=2):
     from soupsuck_b200.kernels import fused_linear_cross_entropy
-    t, h, v = T_TOKENS, HIDDEN, 151936
+    t, h, v = tokens, HIDDEN, 151936
     g = torch.Generator(device=device).manual_seed(4)
     hidden = torch.randn((t, h), device=device, dtype=torch.float16, generator=g).requires_grad_()
     weight = (torch.randn((v, h), device=device, generator=g) * 0.02).to(torch.float16)
@@ -263,11 +263,11 @@ def ce_benchmark(torch, device, steps):
         loss.sum().backward()
         hidden.grad = None
 
-    for _ in range(2):
+    for _ in range(warm):
         once()
     torch.cuda.synchronize()
     times = []
-    for _ in range(max(3, min(steps, 10))):
+    for _ in range(max(1, min(steps, 10))):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         once()
@@ -278,6 +278,55 @@ def ce_benchmark(torch, device, steps):
     flops = 2 * t * v * h + 4 * valid * v * h
     return {"tokens_per_s": t / sec, "ms_per_step": 1000 * sec, "tflops": flops / sec / 1e12,
             "config": {"tokens": t, "vocab": v, "hidden": h, "labelled": valid}}
+
+
+def kernel_case(args, torch):
+    """--kernel-case: a small, self-checking launch of one kernel family for ncu
+    captures (a few launches, well under a GB on the device).  Exits 0 only if
+    no kernel reported a device error."""
+    from soupsuck_b200 import _lib
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    t = args.tokens
+    if args.kernel_case in ("nf4_fwd", "nf4_dx"):
+        from soupsuck_b200.kernels.nf4_gemm import nf4_linear_raw
+        from soupsuck_b200.quantize import quantize_nf4
+        g = torch.Generator(device=device).manual_seed(0)
+        n, k = args.case_n, args.case_k
+        w = (torch.randn((n, k), device=device, generator=g) * 0.02).to(torch.float16)
+        packed, st = quantize_nf4(w)
+        za = torch.randn((t, RANK_R), device=device, dtype=torch.float16, generator=g)
+        if args.kernel_case == "nf4_fwd":
+            x = torch.randn((t, k), device=device, dtype=torch.float16, generator=g)
+            lb = (torch.randn((n, RANK_R), device=device, generator=g) * 0.01).half()
+            call = lambda: nf4_linear_raw(x, packed, st, lora_a=za, lora_b=lb)
+        else:
+            x = torch.randn((t, n), device=device, dtype=torch.float16, generator=g)
+            la = (torch.randn((k, RANK_R), device=device, generator=g) * 0.01).half()
+            call = lambda: nf4_linear_raw(x, packed, st, transpose=True, lora_a=za, lora_b=la)
+        for _ in range(args.warmup + args.steps):
+            call()
+    elif args.kernel_case == "gemm_pass":
+        layer = build_layer(torch, device, seed=0)
+        gemm_roofline(torch, layer, device, t, passes=args.steps, warm=args.warmup)
+    elif args.kernel_case == "layer":
+        layer = build_layer(torch, device, seed=0)
+        gen = torch.Generator(device=device).manual_seed(1000)
+        inp = {name: torch.randn(shp, device=device, dtype=torch.float16, generator=gen)
+               for name, shp in input_shapes(t).items()}
+        for name in ("residual", "attn", "act", "mlp_prev"):
+            inp[name].requires_grad_()
+        for _ in range(args.warmup + args.steps):
+            for name in ("residual", "attn", "act", "mlp_prev"):
+                inp[name].grad = None
+            layer_step(torch, layer, inp)
+    elif args.kernel_case == "ce":
+        ce_benchmark(torch, device, args.steps, tokens=t, warm=args.warmup)
+    torch.cuda.synchronize()
+    err = _lib.take_device_error(device)
+    print(json.dumps({"kernel_case": args.kernel_case, "tokens": t, "device_error": err,
+                      "launches": _lib.launch_count()}))
+    return 1 if err else 0
 
 
 # ------------------------------------------------------------------ main
@@ -292,9 +341,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ce", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--kernel-case", choices=["nf4_fwd", "nf4_dx", "gemm_pass", "layer", "ce"],
+                    help="run a small launch of one kernel family (for ncu) instead of the bench")
+    ap.add_argument("--case-n", type=int, default=INTER)
+    ap.add_argument("--case-k", type=int, default=HIDDEN)
     args = ap.parse_args()
 
     import torch
+
+    if args.kernel_case:
+        return kernel_case(args, torch)
 
     if args.impl == "reference":
         return run_reference(args, torch)

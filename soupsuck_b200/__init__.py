@@ -1,0 +1,15 @@
+"""soupsuck_b200: the NF4 QLoRA hot path of Khasuetolog/soupsuck on sm_100a.
+
+``apply()`` is the drop-in for the reference's ``solution.apply()``
+(solution/__init__.py:16-20): it registers lazy, idempotent patches and
+imports nothing heavy.  The kernels themselves live in
+``soupsuck_b200.kernels`` (reference kernel API) over the C ABI in
+``include/soupsuck_b200.h``.
+"""
+
+
+def apply():
+    """Register patches lazily; repeated calls leave installed methods intact."""
+    from .patch import install
+
+    install()
