@@ -58,6 +58,34 @@ def step_flops(m):
     return sum(sum(proj_flops(m, n, k, RANK_R)) for _, n, k in PROJ)
 
 
+def nf4_weight_bytes(n, k):
+    """Packed codes, uint8 absmax per 64, fp32 absmax2 per 16384 elements, code table, offset."""
+    return n * k // 2 + n * k // 64 + 4 * ((n * k + 16383) // 16384) + 1024 + 4
+
+
+def pass_bytes(m):
+    """Algorithmic HBM bytes of the 14-launch GEMM pass: per launch the weight, the
+    activation read, the output written, the LoRA factor and the rank-r operand."""
+    total = 0
+    for _, n, k in PROJ:
+        one = nf4_weight_bytes(n, k) + 2 * m * k + 2 * m * n + 2 * RANK_R * (k + n) + 2 * m * RANK_R
+        total += 2 * one
+    return total
+
+
+TRAFFIC_PROFILE = ROOT / "profiles" / "nf4_gemm_pass_t3300_traffic.md"
+
+
+def measured_pass_traffic(m):
+    """DRAM bytes of one GEMM pass from the committed ncu capture (T=3300 only)."""
+    if m != T_TOKENS or not TRAFFIC_PROFILE.exists():
+        return None
+    for line in TRAFFIC_PROFILE.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_pass:"):
+            return int(line.split(":")[1])
+    return None
+
+
 def measured_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -539,7 +567,9 @@ def main():
                 "ms_per_step": 1000 * e2e_sec},
         "gpu_launches": int(launches_per_step) * args.steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_burst, "unit": "TFLOP/s",
-                     "frac": achieved / peak_burst, "traffic": None,
+                     "frac": achieved / peak_burst, "traffic": measured_pass_traffic(t),
+                     "traffic_unit": "DRAM bytes per pass of the 14 launches (ncu, profiles/nf4_gemm_pass_t3300_traffic.md)",
+                     "algorithmic_bytes": pass_bytes(t),
                      "kernel": "gemm_kernel<NF4> fwd+dX, LoRA fused",
                      "peak_source": f"{peak_kind} bf16 dense burst (MEASURED_PEAKS.json)",
                      "launches": glaunch, "ms_per_pass": 1000 * gsec},
