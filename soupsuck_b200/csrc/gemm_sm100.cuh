@@ -531,7 +531,10 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
           const uint32_t ph = (it / STAGES) & 1;
           const bool main_step = u.k0 + ls < u.k1;
           if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
-          if (C::kNF4 && main_step) {
+          // Every step, the LoRA step included, waits for the decoder group's arrival:
+          // otherwise the stage could be refilled before a lagging group has seen
+          // this phase of full[s], and its parity wait would then alias the next phase.
+          if (C::kNF4) {
             if (!mbar_wait(&decoded[s], ph, kErrWaitDecoded, abort_flag)) { ok = false; break; }
           }
           tc_fence_after();
