@@ -138,10 +138,11 @@ __device__ __forceinline__ void nf4_table(float scale, uint32_t (&L)[4], uint32_
   }
 }
 
-// Decode one 64-element block (packed bytes 0-15 at `raw_lo`, 16-31 at `raw_hi`) into a 128-byte
-// swizzled SMEM row at `dst` (row index `r` inside its 8-row swizzle atom).
-__device__ __forceinline__ void nf4_decode_row(const uint8_t* raw_lo, const uint8_t* raw_hi,
-                                               uint8_t* dst, int r, float scale, bool valid) {
+// Decode one 64-element block given as its 32 packed bytes (p0 = bytes 0-15, p1 = 16-31)
+// into a 128-byte swizzled SMEM row at `dst` (row index `r` inside its 8-row swizzle atom);
+// an invalid block (outside the weight) is written as zeros.
+__device__ __forceinline__ void nf4_decode_words(uint4 p0, uint4 p1, uint8_t* dst, int r, float scale,
+                                                 bool valid) {
   const uint32_t swz = static_cast<uint32_t>(r & 7);
   if (!valid) {
 #pragma unroll
@@ -150,8 +151,6 @@ __device__ __forceinline__ void nf4_decode_row(const uint8_t* raw_lo, const uint
     }
     return;
   }
-  const uint4 p0 = *reinterpret_cast<const uint4*>(raw_lo);
-  const uint4 p1 = *reinterpret_cast<const uint4*>(raw_hi);
   uint32_t L[4], H[4];
   nf4_table(scale, L, H);
   const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
@@ -159,6 +158,14 @@ __device__ __forceinline__ void nf4_decode_row(const uint8_t* raw_lo, const uint
   for (int c = 0; c < 8; ++c) {
     *reinterpret_cast<uint4*>(dst + ((c ^ swz) << 4)) = nf4_expand8(words[c], L, H);
   }
+}
+
+// Same, reading the packed bytes from shared memory (`raw_lo`: bytes 0-15, `raw_hi`: 16-31).
+__device__ __forceinline__ void nf4_decode_row(const uint8_t* raw_lo, const uint8_t* raw_hi,
+                                               uint8_t* dst, int r, float scale, bool valid) {
+  const uint4 p0 = valid ? *reinterpret_cast<const uint4*>(raw_lo) : make_uint4(0, 0, 0, 0);
+  const uint4 p1 = valid ? *reinterpret_cast<const uint4*>(raw_hi) : make_uint4(0, 0, 0, 0);
+  nf4_decode_words(p0, p1, dst, r, scale, valid);
 }
 
 __device__ __forceinline__ float nf4_scale(const Params& p, int64_t blk, float off) {
@@ -394,6 +401,144 @@ __device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, volatil
   return ok;
 }
 
+// ------------------------------------------------------------ epilogue role
+// Warps 4..7: drain each finished accumulator from TMEM (lanes 32 * (warp % 4)),
+// run the epilogue and release the buffer; stream-K partial tiles are parked in
+// the caller-provided partial slots and the last contributor finishes the tile.
+template <int EMODE, int MSUB, int BN>
+__device__ __forceinline__ void run_epilogue_role(const Params& p, uint32_t tmem_base, uint64_t* acc_full,
+                                                  uint64_t* acc_empty, uint64_t* epi_mb,
+                                                  volatile int* abort_flag, volatile int* last_flag,
+                                                  int warp, int lane, int num_tiles, int rows_valid) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int etid = (warp - 4) * 32 + lane;
+    const int64_t total = static_cast<int64_t>(num_tiles) * p.k_blocks;
+    uint32_t tl = 0, epi_phase = 0;
+    int uidx = 0;
+    UnitIter iter(p, num_tiles);
+    Unit u;
+    while (iter.next(u)) {
+      const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
+      const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
+      if (m0 >= rows_valid) continue;
+      const int buf = tl & 1;
+      const uint32_t aph = (tl >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * MSUB * BN;
+      if (u.k0 == 0 && u.k1 == p.k_blocks) {
+#pragma unroll 1
+        for (int ms = 0; ms < MSUB; ++ms) {
+          const int row = m0 + ms * kTileRows + q * 32 + lane;
+          EpiState st;
+          epilogue_begin<EMODE>(p, st, row, rows_valid);
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tacc + ms * BN + c * 32, v);
+            tmem_ld_wait();
+            epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+          }
+          epilogue_end<EMODE>(p, st, row, nt, rows_valid);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+      } else {
+        // Stream-K partial tile: park the fp32 accumulator in this CTA's slot,
+        // release TMEM, then let the last contributor to arrive sum every slot
+        // in CTA order (deterministic) and run the epilogue.
+        const int slot = uidx == 0 ? 0 : 1;
+        // Slot layout is thread-major ([ms][chunk][j][etid] float4) so each warp
+        // writes and later reads 512 contiguous bytes per instruction.
+        constexpr int kSlotF4 = MSUB * (BN / 32) * 8 * 128;  // float4 per slot
+        float4* mine = reinterpret_cast<float4*>(p.partials) + (static_cast<int64_t>(blockIdx.x) * 2 + slot) * kSlotF4;
+#pragma unroll 1
+        for (int ms = 0; ms < MSUB; ++ms) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tacc + ms * BN + c * 32, v);
+            tmem_ld_wait();
+            float4* dst = mine + ((ms * (BN / 32) + c) * 8) * 128 + etid;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              __stcg(dst + j * 128, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        __threadfence();
+        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+        const int64_t it0 = static_cast<int64_t>(u.tile) * p.k_blocks;
+        const int c_lo = sk_owner(it0, total, gridDim.x);
+        const int c_hi = sk_owner(it0 + p.k_blocks - 1, total, gridDim.x);
+        if (etid == 0) {
+          const int prev = atomicAdd(p.counters + u.tile, 1);
+          *last_flag = (prev == c_hi - c_lo) ? 1 : 0;
+        }
+        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+        const bool last = *last_flag != 0;
+        // Every thread has read the flag before it can be rewritten.
+        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+        if (last) {
+          __threadfence();
+#pragma unroll 1
+          for (int ms = 0; ms < MSUB; ++ms) {
+            const int lrow = ms * kTileRows + q * 32 + lane;
+            const int row = m0 + lrow;
+            EpiState st;
+            epilogue_begin<EMODE>(p, st, row, rows_valid);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              float sum[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+              const int64_t off = static_cast<int64_t>((ms * (BN / 32) + c) * 8) * 128 + etid;
+              // Contributors are summed in CTA order; their loads are issued
+              // in batches of four so the L2 round trips overlap.
+              for (int cc = c_lo; cc <= c_hi; cc += 4) {
+                float4 x[4][8];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                  const int ci = cc + b;
+                  if (ci <= c_hi) {
+                    const int64_t first_tile = (total * ci / gridDim.x) / p.k_blocks;
+                    const int cslot = first_tile == u.tile ? 0 : 1;
+                    const float4* src = reinterpret_cast<const float4*>(p.partials) +
+                                        (static_cast<int64_t>(ci) * 2 + cslot) * kSlotF4 + off;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) x[b][j] = __ldcg(src + j * 128);
+                  }
+                }
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                  if (cc + b <= c_hi) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                      sum[4 * j] += x[b][j].x; sum[4 * j + 1] += x[b][j].y;
+                      sum[4 * j + 2] += x[b][j].z; sum[4 * j + 3] += x[b][j].w;
+                    }
+                  }
+                }
+              }
+              uint32_t v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(sum[j]);
+              epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+            }
+            epilogue_end<EMODE>(p, st, row, nt, rows_valid);
+          }
+          if (etid == 0) p.counters[u.tile] = 0;  // ready for the next launch
+        }
+      }
+      ++tl;
+      ++uidx;
+    }
+}
+
 // ------------------------------------------------------------ the kernel
 template <int BMODE, int EMODE, int MSUB, int BN, int STAGES>
 __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
@@ -574,133 +719,8 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
       mbar_wait(drain, 0, kErrWaitDrain, &no_abort);
     }
   } else if (warp >= 4 && warp < 8) {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int etid = (warp - 4) * 32 + lane;
-    const int64_t total = static_cast<int64_t>(num_tiles) * p.k_blocks;
-    uint32_t tl = 0, epi_phase = 0;
-    int uidx = 0;
-    UnitIter iter(p, num_tiles);
-    Unit u;
-    while (iter.next(u)) {
-      const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
-      const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
-      if (m0 >= rows_valid) continue;
-      const int buf = tl & 1;
-      const uint32_t aph = (tl >> 1) & 1;
-      if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) break;
-      tc_fence_after();
-      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * MSUB * BN;
-      if (u.k0 == 0 && u.k1 == p.k_blocks) {
-#pragma unroll 1
-        for (int ms = 0; ms < MSUB; ++ms) {
-          const int row = m0 + ms * kTileRows + q * 32 + lane;
-          EpiState st;
-          epilogue_begin<EMODE>(p, st, row, rows_valid);
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(tacc + ms * BN + c * 32, v);
-            tmem_ld_wait();
-            epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
-          }
-          epilogue_end<EMODE>(p, st, row, nt, rows_valid);
-        }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[buf]);
-      } else {
-        // Stream-K partial tile: park the fp32 accumulator in this CTA's slot,
-        // release TMEM, then let the last contributor to arrive sum every slot
-        // in CTA order (deterministic) and run the epilogue.
-        const int slot = uidx == 0 ? 0 : 1;
-        // Slot layout is thread-major ([ms][chunk][j][etid] float4) so each warp
-        // writes and later reads 512 contiguous bytes per instruction.
-        constexpr int kSlotF4 = MSUB * (BN / 32) * 8 * 128;  // float4 per slot
-        float4* mine = reinterpret_cast<float4*>(p.partials) + (static_cast<int64_t>(blockIdx.x) * 2 + slot) * kSlotF4;
-#pragma unroll 1
-        for (int ms = 0; ms < MSUB; ++ms) {
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(tacc + ms * BN + c * 32, v);
-            tmem_ld_wait();
-            float4* dst = mine + ((ms * (BN / 32) + c) * 8) * 128 + etid;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              __stcg(dst + j * 128, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
-            }
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[buf]);
-        __threadfence();
-        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
-        const int64_t it0 = static_cast<int64_t>(u.tile) * p.k_blocks;
-        const int c_lo = sk_owner(it0, total, gridDim.x);
-        const int c_hi = sk_owner(it0 + p.k_blocks - 1, total, gridDim.x);
-        if (etid == 0) {
-          const int prev = atomicAdd(p.counters + u.tile, 1);
-          *last_flag = (prev == c_hi - c_lo) ? 1 : 0;
-        }
-        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
-        const bool last = *last_flag != 0;
-        // Every thread has read the flag before it can be rewritten.
-        if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
-        if (last) {
-          __threadfence();
-#pragma unroll 1
-          for (int ms = 0; ms < MSUB; ++ms) {
-            const int lrow = ms * kTileRows + q * 32 + lane;
-            const int row = m0 + lrow;
-            EpiState st;
-            epilogue_begin<EMODE>(p, st, row, rows_valid);
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-              float sum[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
-              const int64_t off = static_cast<int64_t>((ms * (BN / 32) + c) * 8) * 128 + etid;
-              // Contributors are summed in CTA order; their loads are issued
-              // in batches of four so the L2 round trips overlap.
-              for (int cc = c_lo; cc <= c_hi; cc += 4) {
-                float4 x[4][8];
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                  const int ci = cc + b;
-                  if (ci <= c_hi) {
-                    const int64_t first_tile = (total * ci / gridDim.x) / p.k_blocks;
-                    const int cslot = first_tile == u.tile ? 0 : 1;
-                    const float4* src = reinterpret_cast<const float4*>(p.partials) +
-                                        (static_cast<int64_t>(ci) * 2 + cslot) * kSlotF4 + off;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) x[b][j] = __ldcg(src + j * 128);
-                  }
-                }
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                  if (cc + b <= c_hi) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                      sum[4 * j] += x[b][j].x; sum[4 * j + 1] += x[b][j].y;
-                      sum[4 * j + 2] += x[b][j].z; sum[4 * j + 3] += x[b][j].w;
-                    }
-                  }
-                }
-              }
-              uint32_t v[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(sum[j]);
-              epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
-            }
-            epilogue_end<EMODE>(p, st, row, nt, rows_valid);
-          }
-          if (etid == 0) p.counters[u.tile] = 0;  // ready for the next launch
-        }
-      }
-      ++tl;
-      ++uidx;
-    }
+    run_epilogue_role<EMODE, MSUB, BN>(p, tmem_base, acc_full, acc_empty, epi_mb, abort_flag, last_flag,
+                                       warp, lane, num_tiles, rows_valid);
   } else if (C::kNF4 && warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders
     // Group g decodes the k-steps whose global index has parity g.  Each thread

@@ -19,6 +19,9 @@
 // fragments from 16-byte (project) or 4-byte (reduce) vector loads.
 #pragma once
 
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace sb {
@@ -34,63 +37,6 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 
 __device__ __forceinline__ uint4 ldg16_or_zero(const __half* p, bool ok) {
   return ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
-}
-
-// ------------------------------------------------------------------ project
-// One CTA = 4 warps = one 16-row tile of X; warp w reduces the w-th quarter of K
-// in 32-element chunks; the four partial tiles are summed through shared memory.
-template <int R>
-__global__ void __launch_bounds__(128) project_kernel(
-    const __half* __restrict__ X, int64_t M, int64_t K, const __half* __restrict__ W,
-    float scale_rows, __half* __restrict__ out_rows, int ld_rows, float scale_t,
-    __half* __restrict__ out_t, int64_t ldt) {
-  constexpr int NT = R / 8;
-  __shared__ float red[4][16][R];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 16;
-  const int64_t chunks = K / 32;
-  const int64_t c_begin = chunks * warp / 4, c_end = chunks * (warp + 1) / 4;
-  float acc[NT][4];
-#pragma unroll
-  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-  const bool r0ok = m0 + g < M, r1ok = m0 + g + 8 < M;
-  const __half* x0 = X + (m0 + g) * K + 8 * t;
-  const __half* x1 = X + (m0 + g + 8) * K + 8 * t;
-  const __half* wrow = W + static_cast<int64_t>(g) * K + 8 * t;
-#pragma unroll 2
-  for (int64_t c = c_begin; c < c_end; ++c) {
-    const int64_t k0 = c * 32;
-    const uint4 xa = ldg16_or_zero(x0 + k0, r0ok);
-    const uint4 xb = ldg16_or_zero(x1 + k0, r1ok);
-    const uint32_t a_lo[4] = {xa.x, xb.x, xa.y, xb.y};
-    const uint32_t a_hi[4] = {xa.z, xb.z, xa.w, xb.w};
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const uint4 w = __ldg(reinterpret_cast<const uint4*>(wrow + static_cast<int64_t>(8 * j) * K + k0));
-      mma16816(acc[j], a_lo, w.x, w.y);
-      mma16816(acc[j], a_hi, w.z, w.w);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < NT; ++j) {
-    red[warp][g][8 * j + 2 * t] = acc[j][0];
-    red[warp][g][8 * j + 2 * t + 1] = acc[j][1];
-    red[warp][g + 8][8 * j + 2 * t] = acc[j][2];
-    red[warp][g + 8][8 * j + 2 * t + 1] = acc[j][3];
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 16 * R; i += 128) {
-    const int row = i / R, col = i % R;
-    const float v = red[0][row][col] + red[1][row][col] + red[2][row][col] + red[3][row][col];
-    const int64_t m = m0 + row;
-    if (m < M) {
-      if (out_rows) out_rows[m * ld_rows + col] = __float2half_rn(v * scale_rows);
-      if (out_t) out_t[static_cast<int64_t>(col) * ldt + m] = __float2half_rn(v * scale_t);
-    } else if (out_t && m < ldt) {
-      out_t[static_cast<int64_t>(col) * ldt + m] = __float2half_rn(0.0f);  // zero pad for the reduction
-    }
-  }
 }
 
 // ------------------------------------------------------------------ reduce
@@ -160,6 +106,228 @@ __global__ void reduce_finalize_kernel(const float* __restrict__ partial, int sp
   st_from_f32(out, odt, transpose ? c * r + j : j * Wd + c, acc);
 }
 
+// ------------------------------------------------------------------ streamed variants
+// The two kernels above keep few bytes in flight (4-byte loads in the reduction,
+// one 16-row tile of 4 warps in the projection).  The streamed variants below
+// are what the C entry points use for aligned shapes: they move 16-byte pieces
+// with many loads in flight per thread, so both run close to HBM bandwidth.
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;  // src-size 0 zero-fills the 16 bytes
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+// project2: one CTA = 8 warps = one 16-row tile of X; warp w reduces the w-th
+// eighth of K, loading kUnroll 32-element chunks of both rows before its MMAs.
+template <int R>
+__global__ void __launch_bounds__(256) project2_kernel(
+    const __half* __restrict__ X, int64_t M, int64_t K, const __half* __restrict__ W,
+    float scale_rows, __half* __restrict__ out_rows, int ld_rows, float scale_t,
+    __half* __restrict__ out_t, int64_t ldt) {
+  constexpr int NT = R / 8;
+  constexpr int kWarps = 8;
+  constexpr int kUnroll = 4;
+  __shared__ float red[kWarps][16][R + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 16;
+  const int64_t chunks = K / 32;
+  const int64_t c_begin = chunks * warp / kWarps, c_end = chunks * (warp + 1) / kWarps;
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  const bool r0ok = m0 + g < M, r1ok = m0 + g + 8 < M;
+  const __half* x0 = X + (m0 + g) * K + 8 * t;
+  const __half* x1 = X + (m0 + g + 8) * K + 8 * t;
+  const __half* wrow = W + static_cast<int64_t>(g) * K + 8 * t;
+  for (int64_t c = c_begin; c < c_end; c += kUnroll) {
+    uint4 xa[kUnroll], xb[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const bool in = c + u < c_end;
+      const int64_t k0 = (c + u) * 32;
+      xa[u] = ldg16_or_zero(x0 + k0, in && r0ok);
+      xb[u] = ldg16_or_zero(x1 + k0, in && r1ok);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (c + u < c_end) {
+        const int64_t k0 = (c + u) * 32;
+        const uint32_t a_lo[4] = {xa[u].x, xb[u].x, xa[u].y, xb[u].y};
+        const uint32_t a_hi[4] = {xa[u].z, xb[u].z, xa[u].w, xb[u].w};
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const uint4 w = __ldg(reinterpret_cast<const uint4*>(wrow + static_cast<int64_t>(8 * j) * K + k0));
+          mma16816(acc[j], a_lo, w.x, w.y);
+          mma16816(acc[j], a_hi, w.z, w.w);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    red[warp][g][8 * j + 2 * t] = acc[j][0];
+    red[warp][g][8 * j + 2 * t + 1] = acc[j][1];
+    red[warp][g + 8][8 * j + 2 * t] = acc[j][2];
+    red[warp][g + 8][8 * j + 2 * t + 1] = acc[j][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * R; i += blockDim.x) {
+    const int row = i / R, col = i % R;
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += red[w][row][col];
+    const int64_t m = m0 + row;
+    if (m < M) {
+      if (out_rows) out_rows[m * ld_rows + col] = __float2half_rn(v * scale_rows);
+      if (out_t) out_t[static_cast<int64_t>(col) * ldt + m] = __float2half_rn(v * scale_t);
+    } else if (out_t && m < ldt) {
+      out_t[static_cast<int64_t>(col) * ldt + m] = __float2half_rn(0.0f);  // zero pad for the reduction
+    }
+  }
+}
+
+// reduce2: CTA = 256 output columns (8 warps x 32) over rows [split * rows_per_split, ...).
+// 32-row tiles of Q (16 KB) and Pt (R x 64 B) are staged with cp.async in a
+// kStages ring; fragments come from ldmatrix (Q transposed).  Shared layouts are
+// XOR-swizzled on 16-byte chunks so every ldmatrix phase hits 32 distinct banks:
+// Q row k (512 B): chunk c stored at c ^ (k & 7); Pt row j (64 B): c at c ^ ((j >> 1) & 3).
+// Requires Wd % 8 == 0, 16-byte aligned Q and Pt, ldp % 16 == 0.
+constexpr int kRedCols = 256, kRedRows = 32, kRedStages = 4;
+
+template <int R>
+struct Red2Smem {
+  static constexpr int kQBytes = kRedRows * kRedCols * 2;  // 16 KB
+  static constexpr int kPBytes = R * kRedRows * 2;         // R x 64 B
+  static constexpr int kStage = kQBytes + kPBytes;
+  static constexpr int kBytes = kRedStages * kStage;
+};
+
+template <int R>
+__global__ void __launch_bounds__(256) reduce2_kernel(
+    const __half* __restrict__ Pt, int64_t ldp, const __half* __restrict__ Q, int64_t M,
+    int64_t Wd, int64_t rows_per_split, float* __restrict__ partial) {
+  using S = Red2Smem<R>;
+  constexpr int MT = R / 16;
+  extern __shared__ __align__(128) uint8_t red_smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kRedCols;
+  const int64_t mb = static_cast<int64_t>(blockIdx.y) * rows_per_split;
+  int64_t me = mb + rows_per_split;
+  if (me > ldp) me = ldp;
+  const int ntiles = me > mb ? static_cast<int>((me - mb + kRedRows - 1) / kRedRows) : 0;
+  const uint32_t sbase = smem_addr(red_smem);
+
+  auto issue = [&](int tile) {
+    const int slot = tile % kRedStages;
+    const uint32_t qs = sbase + slot * S::kStage;
+    const uint32_t ps = qs + S::kQBytes;
+    const int64_t r0 = mb + static_cast<int64_t>(tile) * kRedRows;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int row = (tid >> 5) + 8 * u, chunk = tid & 31;
+      const int64_t m = r0 + row, col = c0 + chunk * 8;
+      const bool ok = m < M && col < Wd;
+      cp_async16(qs + row * 512 + ((chunk ^ (row & 7)) << 4), ok ? Q + m * Wd + col : Q, ok);
+    }
+    for (int i = tid; i < 4 * R; i += 256) {
+      const int j = i >> 2, chunk = i & 3;
+      const int64_t tok = r0 + chunk * 8;
+      const bool ok = tok < ldp;
+      cp_async16(ps + j * 64 + ((chunk ^ ((j >> 1) & 3)) << 4), ok ? Pt + j * ldp + tok : Pt, ok);
+    }
+  };
+
+  float acc[MT][4][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int n = 0; n < 4; ++n) acc[i][n][0] = acc[i][n][1] = acc[i][n][2] = acc[i][n][3] = 0.0f;
+
+#pragma unroll
+  for (int s = 0; s < kRedStages - 1; ++s) {
+    if (s < ntiles) issue(s);
+    cp_async_commit();
+  }
+  const int mat = lane >> 3, r8 = lane & 7;
+  for (int tile = 0; tile < ntiles; ++tile) {
+    cp_async_wait<kRedStages - 2>();
+    __syncthreads();
+    if (tile + kRedStages - 1 < ntiles) issue(tile + kRedStages - 1);
+    cp_async_commit();
+    const int slot = tile % kRedStages;
+    const uint32_t qs = sbase + slot * S::kStage;
+    const uint32_t ps = qs + S::kQBytes;
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      uint32_t a[MT][4];
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        const int j = 16 * i + r8 + 8 * (mat & 1);
+        const int chunk = 2 * ks + (mat >> 1);
+        ldsm_x4(ps + j * 64 + ((chunk ^ ((j >> 1) & 3)) << 4), a[i]);
+      }
+      uint32_t b[2][4];
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {
+        const int k = 16 * ks + r8 + 8 * (mat & 1);
+        const int chunk = warp * 4 + 2 * pr + (mat >> 1);
+        ldsm_x4_trans(qs + k * 512 + ((chunk ^ (k & 7)) << 4), b[pr]);
+      }
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          mma16816(acc[i][2 * pr], a[i], b[pr][0], b[pr][1]);
+          mma16816(acc[i][2 * pr + 1], a[i], b[pr][2], b[pr][3]);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+  float* out = partial + static_cast<int64_t>(blockIdx.y) * R * Wd;
+#pragma unroll
+  for (int i = 0; i < MT; ++i) {
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int64_t col = c0 + warp * 32 + 8 * n + 2 * t;
+      if (col < Wd) {
+        const int64_t ra = 16 * i + g;
+        *reinterpret_cast<float2*>(out + ra * Wd + col) = make_float2(acc[i][n][0], acc[i][n][1]);
+        *reinterpret_cast<float2*>(out + (ra + 8) * Wd + col) = make_float2(acc[i][n][2], acc[i][n][3]);
+      }
+    }
+  }
+}
+
+// Split count of reduce2: enough CTAs to fill the GPU twice, at least 64 rows each.
+inline int reduce2_splits(int64_t ldp, int64_t w) {
+  const int64_t col_blocks = (w + kRedCols - 1) / kRedCols;
+  int64_t s = (2 * device_sm_count() + col_blocks - 1) / col_blocks;
+  const int64_t max_s = (ldp + 63) / 64;
+  if (s > max_s) s = max_s;
+  if (s < 1) s = 1;
+  if (s > 4096) s = 4096;
+  return static_cast<int>(s);
+}
+
+inline bool reduce2_ok(const void* pt, const void* q, int64_t w) {
+  return w % 8 == 0 && aligned(pt, 16) && aligned(q, 16);
+}
+
 // ------------------------------------------------------------------ prepare
 // a [r, K] (dtype adt) -> a16 [r, K], at16 [K, r]; b [N, r] (bdt) -> b16 [N, r], bt16 [r, N].
 __global__ void prepare_kernel(const void* __restrict__ a, int adt, const void* __restrict__ b,
@@ -183,6 +351,27 @@ __global__ void prepare_kernel(const void* __restrict__ a, int adt, const void* 
       if (bt16) bt16[j * N + n] = v;
     }
   }
+}
+
+template <int R>
+inline int launch_reduce2(dim3 grid, const __half* P, int64_t ldp, const __half* Q, int64_t m, int64_t w,
+                          int64_t rows_per_split, float* partial, cudaStream_t st) {
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(reduce2_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Red2Smem<R>::kBytes);
+      if (e != cudaSuccess) return fail(SB_ECUDA, std::string("reduce2 smem attribute: ") + cudaGetErrorString(e));
+      configured[dev] = true;
+    }
+  }
+  reduce2_kernel<R><<<grid, 256, Red2Smem<R>::kBytes, st>>>(P, ldp, Q, m, w, rows_per_split, partial);
+  count_launch();
+  return check_launch("lora_reduce2_kernel");
 }
 
 inline int reduce_splits(int64_t m, int64_t w) {
@@ -217,17 +406,18 @@ int sb_lora_project(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, 
   const __half* W = reinterpret_cast<const __half*>(w);
   __half* orow = reinterpret_cast<__half*>(out_rows);
   __half* ot = reinterpret_cast<__half*>(out_t);
-  if (r == 16) sb::lora::project_kernel<16><<<grid, 128, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
-  else if (r == 32) sb::lora::project_kernel<32><<<grid, 128, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
-  else sb::lora::project_kernel<64><<<grid, 128, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
+  if (r == 16) sb::lora::project2_kernel<16><<<grid, 256, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
+  else if (r == 32) sb::lora::project2_kernel<32><<<grid, 256, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
+  else sb::lora::project2_kernel<64><<<grid, 256, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
   sb::count_launch();
-  return sb::check_launch("lora_project_kernel");
+  return sb::check_launch("lora_project2_kernel");
 }
 
 size_t sb_lora_reduce_workspace_bytes(int64_t m, int64_t w, int r) {
   if (m <= 0 || w <= 0 || r <= 0) return 0;
   const int64_t ldp = (m + 15) / 16 * 16;  // the zero-padded row count the reduction runs over
-  return static_cast<size_t>(sb::lora::reduce_splits(ldp, w)) * r * w * sizeof(float);
+  const int64_t splits = std::max(sb::lora::reduce_splits(ldp, w), sb::lora::reduce2_splits(ldp, w));
+  return static_cast<size_t>(splits) * r * w * sizeof(float);
 }
 
 int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m, int64_t w, int r,
@@ -246,20 +436,36 @@ int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m
   }
   SB_REQUIRE(pt && q, "NULL pointer argument");
   SB_REQUIRE(sb::aligned(pt, 4) && sb::aligned(q, 4), "pt and q must be 4-byte aligned");
-  const int splits = sb::lora::reduce_splits(ldp, w);
-  const size_t need = static_cast<size_t>(splits) * r * w * sizeof(float);
-  if (!workspace || workspace_bytes < need) return sb::fail(SB_EWORKSPACE, "LoRA reduce workspace too small");
-  int64_t rows_per_split = (ldp + splits - 1) / splits;
-  rows_per_split = (rows_per_split + 15) / 16 * 16;
-  dim3 grid(static_cast<unsigned>((w + 127) / 128), static_cast<unsigned>(splits));
   float* partial = static_cast<float*>(workspace);
   const __half* P = reinterpret_cast<const __half*>(pt);
   const __half* Q = reinterpret_cast<const __half*>(q);
-  if (r == 16) sb::lora::reduce_partial_kernel<16><<<grid, 256, 0, st>>>(P, ldp, Q, m, w, rows_per_split, partial);
-  else if (r == 32) sb::lora::reduce_partial_kernel<32><<<grid, 256, 0, st>>>(P, ldp, Q, m, w, rows_per_split, partial);
-  else sb::lora::reduce_partial_kernel<64><<<grid, 256, 0, st>>>(P, ldp, Q, m, w, rows_per_split, partial);
-  sb::count_launch();
-  if (int rc = sb::check_launch("lora_reduce_partial_kernel")) return rc;
+  int splits = 0;
+  if (sb::lora::reduce2_ok(pt, q, w)) {
+    splits = sb::lora::reduce2_splits(ldp, w);
+    int64_t rows_per_split = (ldp + splits - 1) / splits;
+    rows_per_split = (rows_per_split + sb::lora::kRedRows - 1) / sb::lora::kRedRows * sb::lora::kRedRows;
+    splits = static_cast<int>((ldp + rows_per_split - 1) / rows_per_split);
+    const size_t need = static_cast<size_t>(splits) * r * w * sizeof(float);
+    if (!workspace || workspace_bytes < need) return sb::fail(SB_EWORKSPACE, "LoRA reduce workspace too small");
+    dim3 grid(static_cast<unsigned>((w + sb::lora::kRedCols - 1) / sb::lora::kRedCols), static_cast<unsigned>(splits));
+    int rc = SB_OK;
+    if (r == 16) rc = sb::lora::launch_reduce2<16>(grid, P, ldp, Q, m, w, rows_per_split, partial, st);
+    else if (r == 32) rc = sb::lora::launch_reduce2<32>(grid, P, ldp, Q, m, w, rows_per_split, partial, st);
+    else rc = sb::lora::launch_reduce2<64>(grid, P, ldp, Q, m, w, rows_per_split, partial, st);
+    if (rc) return rc;
+  } else {
+    splits = sb::lora::reduce_splits(ldp, w);
+    const size_t need = static_cast<size_t>(splits) * r * w * sizeof(float);
+    if (!workspace || workspace_bytes < need) return sb::fail(SB_EWORKSPACE, "LoRA reduce workspace too small");
+    int64_t rows_per_split = (ldp + splits - 1) / splits;
+    rows_per_split = (rows_per_split + 15) / 16 * 16;
+    dim3 grid(static_cast<unsigned>((w + 127) / 128), static_cast<unsigned>(splits));
+    if (r == 16) sb::lora::reduce_partial_kernel<16><<<grid, 256, 0, st>>>(P, ldp, Q, m, w, rows_per_split, partial);
+    else if (r == 32) sb::lora::reduce_partial_kernel<32><<<grid, 256, 0, st>>>(P, ldp, Q, m, w, rows_per_split, partial);
+    else sb::lora::reduce_partial_kernel<64><<<grid, 256, 0, st>>>(P, ldp, Q, m, w, rows_per_split, partial);
+    sb::count_launch();
+    if (int rc = sb::check_launch("lora_reduce_partial_kernel")) return rc;
+  }
   const int64_t total = w * r;
   sb::lora::reduce_finalize_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
       partial, splits, w, r, scale, transpose, out, out_dtype);
