@@ -190,6 +190,16 @@ int sb_ce_forward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* 
                   float* entropy, int64_t* argmax, float* lse, void* workspace,
                   size_t workspace_bytes, void* stream);
 size_t sb_ce_forward_workspace_bytes(int64_t t, int64_t h, int64_t v);
+/* Vocabulary-sharded forward: sb_ce_forward over this rank's rows of the head,
+ * plus row_max[t], the largest (fp16-rounded) logit of the shard, which the
+ * cross-rank merge needs for the global first argmax.  Targets that belong to
+ * another shard are passed as -1: they match no column, so the shard
+ * contributes only its softmax terms (no counterpart in the reference, which
+ * runs on one GPU; the per-shard statistics are those of cross_entropy.py:51-105). */
+int sb_ce_forward_shard(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight,
+                        int64_t v, const int64_t* targets, int64_t ignore_index, float* loss,
+                        float* entropy, int64_t* argmax, float* lse, float* row_max,
+                        void* workspace, size_t workspace_bytes, void* stream);
 /* dhidden[t, h] (dtype dh_dtype) of sum_rows(grad[i] * loss[i]); ignored rows
  * get exact zeros and never touch their (possibly non-finite) grad. */
 int sb_ce_backward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight,

@@ -59,6 +59,7 @@ SIGNATURES = {
     "sb_rmsnorm_weight_grad_workspace_bytes": (_SZ, [_I64, _I64]),
     "sb_ce_forward": (_I32, [_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "sb_ce_forward_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sb_ce_forward_shard": (_I32, [_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sb_ce_backward": (_I32, [_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I32, _P, _SZ, _P]),
     "sb_ce_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sb_ce_check_targets": (_I32, [_P, _I64, _I64, _I64, ctypes.POINTER(_I64), _P]),

@@ -43,7 +43,7 @@ __global__ void ce_merge_kernel(const float* __restrict__ stats, const int* __re
                                 int64_t ld, int n_tiles, const int64_t* __restrict__ targets,
                                 int64_t ignore, int64_t rows, float* __restrict__ loss,
                                 float* __restrict__ entropy, int64_t* __restrict__ argmax,
-                                float* __restrict__ lse_out) {
+                                float* __restrict__ lse_out, float* __restrict__ row_max) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= rows) return;
   float M = -INFINITY, S = 0.0f, T = 0.0f, tz = 0.0f;
@@ -70,6 +70,7 @@ __global__ void ce_merge_kernel(const float* __restrict__ stats, const int* __re
   const int64_t tg = targets[i];
   loss[i] = tg != ignore ? l - tz : 0.0f;
   argmax[i] = arg;
+  if (row_max) row_max[i] = M;
 }
 
 // Single-block stream compaction of labelled rows (deterministic order).
@@ -208,10 +209,10 @@ int sb_ce_check_targets(const int64_t* targets, int64_t t, int64_t v, int64_t ig
   return SB_OK;
 }
 
-int sb_ce_forward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight, int64_t v,
-                  const int64_t* targets, int64_t ignore_index, float* loss, float* entropy,
-                  int64_t* argmax, float* lse, void* workspace, size_t workspace_bytes,
-                  void* stream) {
+static int ce_forward_impl(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight, int64_t v,
+                           const int64_t* targets, int64_t ignore_index, float* loss, float* entropy,
+                           int64_t* argmax, float* lse, float* row_max, void* workspace,
+                           size_t workspace_bytes, void* stream) {
   using namespace sb::gemm;
   SB_REQUIRE(t >= 0 && h > 0 && v > 0, "expected t >= 0, h > 0, v > 0");
   if (t == 0) return SB_OK;
@@ -246,9 +247,26 @@ int sb_ce_forward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* 
   rc = launch<kDenseK, kCeStats, 1, sb::ce::kFwdBN, 4>(ta, tb, ta, ta, p, st, "ce_logits_stats");
   if (rc) return rc;
   sb::ce::ce_merge_kernel<<<static_cast<unsigned>((t + 255) / 256), 256, 0, st>>>(
-      stats, args, t, n_tiles, targets, ignore_index, t, loss, entropy, argmax, lse);
+      stats, args, t, n_tiles, targets, ignore_index, t, loss, entropy, argmax, lse, row_max);
   sb::count_launch();
   return sb::check_launch("ce_merge_kernel");
+}
+
+int sb_ce_forward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight, int64_t v,
+                  const int64_t* targets, int64_t ignore_index, float* loss, float* entropy,
+                  int64_t* argmax, float* lse, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  return ce_forward_impl(hidden, t, h, weight, v, targets, ignore_index, loss, entropy, argmax, lse,
+                         nullptr, workspace, workspace_bytes, stream);
+}
+
+int sb_ce_forward_shard(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight, int64_t v,
+                        const int64_t* targets, int64_t ignore_index, float* loss, float* entropy,
+                        int64_t* argmax, float* lse, float* row_max, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  SB_REQUIRE(t == 0 || row_max != nullptr, "NULL row_max");
+  return ce_forward_impl(hidden, t, h, weight, v, targets, ignore_index, loss, entropy, argmax, lse,
+                         row_max, workspace, workspace_bytes, stream);
 }
 
 int sb_ce_backward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight, int64_t v,
