@@ -357,6 +357,135 @@ def kernel_case(args, torch):
     return 1 if err else 0
 
 
+# ------------------------------------------------------------------ 7B shape sweep
+SWEEP_HIDDEN, SWEEP_INTER, SWEEP_KV = 3584, 18944, 512
+SWEEP_PROJ = [("q", SWEEP_HIDDEN, SWEEP_HIDDEN), ("k", SWEEP_KV, SWEEP_HIDDEN), ("v", SWEEP_KV, SWEEP_HIDDEN),
+              ("o", SWEEP_HIDDEN, SWEEP_HIDDEN), ("gate", SWEEP_INTER, SWEEP_HIDDEN),
+              ("up", SWEEP_INTER, SWEEP_HIDDEN), ("down", SWEEP_HIDDEN, SWEEP_INTER)]
+SWEEP_M = (1, 16, 128, 4096, 16384)
+
+
+def run_sweep(args, torch):
+    """Qwen2.5-7B projection shapes, M in {1, 16, 128, 4096, 16384}, NF4 forward and
+    dX of the seven projections (no LoRA), weights N-split across the ranks with an
+    all-gather of Y and an all-reduce of dX when launched on several GPUs.  Reported
+    per M: whole-job TFLOP/s and the HBM rate of the algorithmic bytes (packed
+    weight + absmax + activations in and out)."""
+    import datetime
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    from soupsuck_b200 import _lib
+    from soupsuck_b200.distributed import allreduce_sum, nf4_row_shard
+    from soupsuck_b200.kernels.nf4_gemm import nf4_linear_raw
+    from soupsuck_b200.quantize import quantize_nf4
+    import torch.distributed as dist
+
+    g = torch.Generator(device=device).manual_seed(0)
+    weights = []
+    for name, n, k in SWEEP_PROJ:
+        w = (torch.randn((n, k), device=device, generator=g) * 0.02).to(torch.float16)
+        packed, st = quantize_nf4(w)
+        del w
+        sh = nf4_row_shard(packed, st, rank, world) if world > 1 else None
+        weights.append((name, n, k, packed, st, sh))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    peak_burst, _, hbm, _ = measured_peaks()
+    results = []
+    for m in SWEEP_M:
+        calls, flops, nbytes = [], 0, 0
+        for name, n, k, packed, st, sh in weights:
+            x = torch.randn((m, k), device=device, dtype=torch.float16, generator=g)
+            dy = torch.randn((m, n), device=device, dtype=torch.float16, generator=g)
+            if sh is None:
+                calls.append(lambda x=x, p=packed, s=st: nf4_linear_raw(x, p, s))
+                calls.append(lambda dy=dy, p=packed, s=st: nf4_linear_raw(dy, p, s, transpose=True))
+            else:
+                rows = sh.row1 - sh.row0
+                dy_loc = dy[:, sh.row0:sh.row1].contiguous()
+                buf = torch.empty((world * m, -(-n // world) + 64), device=device, dtype=torch.float16)
+
+                def fwd(x=x, sh=sh, rows=rows, buf=buf):
+                    y = nf4_linear_raw(x, sh.packed, sh.state)
+                    pad = torch.zeros((m, buf.shape[1]), device=device, dtype=torch.float16)
+                    pad[:, :rows] = y
+                    dist.all_gather_into_tensor(buf, pad)
+                    return buf
+
+                def dxf(dy_loc=dy_loc, sh=sh):
+                    return allreduce_sum(nf4_linear_raw(dy_loc, sh.packed, sh.state, transpose=True))
+
+                calls += [fwd, dxf]
+            flops += 2 * (2 * m * n * k)
+            wbytes = nf4_weight_bytes(n, k)
+            nbytes += 2 * (wbytes + 2 * m * k + 2 * m * n)
+        for _ in range(max(args.warmup, 3)):
+            for c in calls:
+                c()
+        torch.cuda.synchronize()
+        # Single GPU: the pass is replayed from a CUDA graph, so host launch overhead
+        # (which exceeds the kernels' own time at M <= 16) stays out of the timing.
+        graph = None
+        if world == 1 and not args.no_graph:
+            side = torch.cuda.Stream(device)
+            side.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(side):
+                for c in calls:
+                    c()
+            torch.cuda.current_stream(device).wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for c in calls:
+                    c()
+            graph.replay()
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        times = []
+        stream = torch.cuda.current_stream(device)
+        for _ in range(max(3, min(args.steps, 10))):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if graph is not None:
+                graph.replay()
+            else:
+                for c in calls:
+                    c()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) / 1000.0)
+        del graph
+        sec = statistics.median(times)
+        if world > 1:
+            tt = torch.tensor([sec], device=device, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            sec = float(tt.item())
+        results.append({"M": m, "ms_per_pass": 1000 * sec, "tflops": flops / sec / 1e12,
+                        "pct_peak": 100 * flops / sec / 1e12 / peak_burst,
+                        "hbm_gbs": nbytes / sec / 1e9, "pct_hbm": 100 * nbytes / sec / 1e9 / hbm,
+                        "projection_calls": len(calls), "cuda_graph": world == 1 and not args.no_graph})
+    err = _lib.take_device_error(device)
+    if rank == 0:
+        print(json.dumps({"metric": "NF4 dequant-GEMM fwd+dX at Qwen2.5-7B shapes (configs[4])",
+                          "n_gpus": world, "dtype": "f16", "data": "synthetic",
+                          "parallelism": f"N-split x{world}" if world > 1 else "single GPU",
+                          "l2": "flushed before every timed pass", "sweep": results, "device_error": err}),
+              flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -369,6 +498,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ce", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--workload", choices=["layer", "sweep"], default="layer",
+                    help="layer: configs[1] (the headline line); sweep: configs[4] 7B shapes")
     ap.add_argument("--kernel-case", choices=["nf4_fwd", "nf4_dx", "gemm_pass", "layer", "ce"],
                     help="run a small launch of one kernel family (for ncu) instead of the bench")
     ap.add_argument("--case-n", type=int, default=INTER)
@@ -379,6 +510,8 @@ def main():
 
     if args.kernel_case:
         return kernel_case(args, torch)
+    if args.workload == "sweep":
+        return run_sweep(args, torch)
 
     if args.impl == "reference":
         return run_reference(args, torch)

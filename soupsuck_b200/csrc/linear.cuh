@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "gemm_host.cuh"
+#include "nf4_smallm.cuh"
 #include "nf4_dequant.cuh"
 
 namespace sb {
@@ -88,6 +89,11 @@ inline int nf4_linear_fallback(bool dx, const uint16_t* act, int64_t m, const sb
   return check_launch("fallback_gemm_kernel");
 }
 
+// Activations of at most 16 rows take the streaming small-M kernel (weight-read bound).
+inline bool smallm_ok(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
+  return m >= 1 && m <= smallm::kRows && k_in % 64 == 0 && (!dx || n_out % 8 == 0);
+}
+
 inline int nf4_linear(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weight* w,
                       const uint16_t* bias, const uint16_t* lora_a, const uint16_t* lora_b, int r,
                       uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
@@ -102,6 +108,10 @@ inline int nf4_linear(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weig
   const bool tc_rank = (r == 0 || r == 16 || r == 32 || r == 64);
   const bool ptrs_ok = aligned(act, 16) && aligned(w->packed, 16) &&
                        (r == 0 || (aligned(lora_a, 16) && aligned(lora_b, 16)));
+  if (smallm_ok(m, w->n_out, w->k_in, dx) && aligned(act, 16) && aligned(w->packed, 16) &&
+      (r == 0 || (aligned(lora_a, 2) && aligned(lora_b, 2)))) {
+    return smallm::run(dx, act, m, *w, bias, lora_a, lora_b, r, out, workspace, workspace_bytes, st);
+  }
   if (tc_rank && ptrs_ok && gemm::nf4_tc_shape_ok(m, w->n_out, w->k_in, dx)) {
     return gemm::nf4_linear_tc(dx, act, m, *w, bias, lora_a, lora_b, r, out, workspace,
                                workspace_bytes, st);
@@ -116,6 +126,9 @@ extern "C" {
 
 size_t sb_nf4_linear_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in, int dx) {
   if (m <= 0 || n_out <= 0 || k_in <= 0) return 0;
+  if (sb::smallm_ok(m, n_out, k_in, dx != 0)) {
+    return sb::smallm::plan(dx ? n_out : k_in, dx ? k_in : n_out).workspace;
+  }
   // Shapes the tcgen05 path takes (with 16-byte aligned operands, which the
   // caller guarantees) need only its stream-K scratch; others the decoded weight.
   if (!sb::gemm::nf4_tc_shape_ok(m, n_out, k_in, dx != 0)) return static_cast<size_t>(n_out) * k_in * 2;

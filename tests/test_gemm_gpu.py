@@ -112,3 +112,35 @@ def test_empty_rows():
 def test_no_device_timeouts_recorded():
     from soupsuck_b200 import _lib
     assert _lib.take_device_error() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 3584, 3584), (5, 512, 3584), (16, 18944, 3584), (16, 3584, 18944),
+                                   (3, 200, 128), (16, 1536, 1536)])
+def test_small_m_forward_and_dx(m, n, k):
+    """M <= 16 rows take the streaming small-M kernel (fp32 partials over reduction slices)."""
+    from soupsuck_b200.kernels import nf4_matmul
+    packed, st, w16 = _weight(n, k, seed=m + 7)
+    x = torch.randn((m, k), device="cuda", dtype=torch.float16)
+    _gate(nf4_matmul(x, packed, st), O.nf4_linear_forward(np_of(x), w16))
+    if n % 8 == 0:
+        dy = torch.randn((m, n), device="cuda", dtype=torch.float16)
+        _gate(nf4_matmul(dy, packed, st, transpose=True), O.nf4_linear_dx(np_of(dy), w16))
+
+
+@pytest.mark.parametrize("m,r", [(1, 16), (16, 64), (7, 8)])
+def test_small_m_lora_and_bias(m, r):
+    from soupsuck_b200.kernels import nf4_lora_linear
+    n, k = 512, 1536
+    packed, st, w16 = _weight(n, k, seed=r)
+    torch.manual_seed(m)
+    x = torch.randn((m, k), device="cuda", dtype=torch.float16, requires_grad=True)
+    a = ((torch.rand((r, k), device="cuda") * 2 - 1) / math.sqrt(k)).requires_grad_()
+    b = (torch.randn((n, r), device="cuda") * 0.01).requires_grad_()
+    bias = torch.randn(n, device="cuda", dtype=torch.float16)
+    y = nf4_lora_linear(x, packed, st, a, b, 2.0, bias=bias)
+    a16 = np_of(a.detach().half()).astype(np.float64)
+    b16 = np_of(b.detach().half()).astype(np.float64)
+    _gate(y, O.nf4_linear_forward(np_of(x), w16, a16, b16, 2.0, bias=np_of(bias)))
+    dy = torch.randn((m, n), device="cuda", dtype=torch.float16)
+    y.backward(dy)
+    _gate(x.grad, O.nf4_linear_dx(np_of(dy), w16, a16, b16, 2.0))
