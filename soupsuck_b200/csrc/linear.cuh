@@ -91,7 +91,8 @@ inline int nf4_linear_fallback(bool dx, const uint16_t* act, int64_t m, const sb
 
 // Activations of at most 16 rows take the streaming small-M kernel (weight-read bound).
 inline bool smallm_ok(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
-  return m >= 1 && m <= smallm::kRows && k_in % 64 == 0 && (!dx || n_out % 8 == 0);
+  return m >= 1 && m <= smallm::kRows && k_in % 64 == 0 && (!dx || n_out % 8 == 0) &&
+         n_out * k_in < (int64_t(1) << 32);  // byte and block offsets fit 32 bits
 }
 
 inline int nf4_linear(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weight* w,

@@ -30,7 +30,7 @@ namespace smallm {
 constexpr int kCols = 256;     // output columns per CTA
 constexpr int kStep = 64;      // reduction elements per step
 constexpr int kRows = 16;      // activation rows (M <= 16)
-constexpr int kStages = 8, kAhead = kStages - 2;  // see the buffer-reuse argument in the kernel
+constexpr int kStages = 4, kAhead = kStages - 2;  // see the buffer-reuse argument in the kernel
 constexpr int kWTile = kCols * kStep * 2;   // 32 KB decoded weight tile (double-buffered)
 constexpr int kRawTile = kCols * kStep / 2; // 8 KB packed bytes per step
 constexpr int kATile = kRows * kStep * 2;   // 2 KB activation tile
@@ -54,7 +54,7 @@ struct Args {
 };
 
 template <bool DX>
-__global__ void __launch_bounds__(256, 1) nf4_smallm_kernel(const Args a) {
+__global__ void __launch_bounds__(256, 2) nf4_smallm_kernel(const Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* code2_s = reinterpret_cast<float*>(smem + kCodeOff);
@@ -69,27 +69,42 @@ __global__ void __launch_bounds__(256, 1) nf4_smallm_kernel(const Args a) {
   const int64_t bpr = a.k_in / 64;
   const int64_t row_bytes = a.k_in / 2;
 
-  // This thread's decode task at step s: weight row, first byte of its 32-byte block, validity.
-  auto task = [&](int64_t s, int64_t& wrow, int64_t& byte0) -> bool {
-    if constexpr (!DX) {
-      wrow = c0 + tid;
-      byte0 = s * (kStep / 2);
-      return wrow < a.n_out && s * kStep < a.k_in;
-    } else {
-      wrow = s * kStep + (tid & 63);
-      const int64_t col = c0 + 64 * (tid >> 6);
-      byte0 = col / 2;
-      return wrow < a.n_out && col < a.k_in;
-    }
+  // This thread's decode task: one (weight row, 64-block) per step.  Forward: row
+  // c0 + tid, block s (the pointers advance by one block per step); dX: row
+  // s * 64 + tid % 64, block (c0 + 64 * (tid / 64)) / 64 (they advance by 64 rows).
+  // Offsets inside the weight fit 32 bits (checked by the host).
+  const uint8_t* pk;
+  const uint8_t* qk;
+  uint32_t pk_step, qk_step;
+  int64_t row_first;       // weight row of step s0 for this thread
+  bool col_ok;
+  if constexpr (!DX) {
+    row_first = c0 + tid;
+    col_ok = row_first < a.n_out;
+    pk = a.packed + static_cast<uint32_t>(row_first * row_bytes + s0 * (kStep / 2));
+    qk = a.qabs + static_cast<uint32_t>(row_first * bpr + s0);
+    pk_step = kStep / 2;
+    qk_step = 1;
+  } else {
+    row_first = s0 * kStep + (tid & 63);
+    const int64_t col = c0 + 64 * (tid >> 6);
+    col_ok = col < a.k_in;
+    pk = a.packed + static_cast<uint32_t>(row_first * row_bytes + col / 2);
+    qk = a.qabs + static_cast<uint32_t>(row_first * bpr + col / 64);
+    pk_step = static_cast<uint32_t>(kStep * row_bytes);
+    qk_step = static_cast<uint32_t>(kStep * bpr);
+  }
+  auto valid_at = [&](int64_t s) -> bool {
+    if constexpr (!DX) return col_ok;
+    else return col_ok && row_first + (s - s0) * kStep < a.n_out;
   };
   // Issue the cp.async copies of step s: this thread's 32 packed bytes, and for
   // threads 0..127 one 16-byte activation chunk (zero-filled outside the operands).
   const int ar = tid >> 3, ac = tid & 7;
   auto issue = [&](int64_t s) {
     const int st = static_cast<int>((s - s0) % kStages);
-    int64_t wrow, byte0;
-    const bool ok = task(s, wrow, byte0);
-    const uint8_t* src = ok ? a.packed + wrow * row_bytes + byte0 : a.packed;
+    const bool ok = valid_at(s);
+    const uint8_t* src = ok ? pk + static_cast<uint32_t>(s - s0) * pk_step : a.packed;
     const uint32_t dst = smem_addr(smem + kRawOff + st * kRawTile + tid * 32);
     lora::cp_async16(dst, src, ok);
     lora::cp_async16(dst + 16, ok ? src + 16 : src, ok);
@@ -101,10 +116,10 @@ __global__ void __launch_bounds__(256, 1) nf4_smallm_kernel(const Args a) {
     }
   };
   // Scale inputs of step s (absmax byte, absmax2 value), kept two steps ahead in registers.
+  const uint32_t q_base = static_cast<uint32_t>(qk - a.qabs);
   auto scale_in = [&](int64_t s, uint32_t& q, float& a2) {
-    int64_t wrow, byte0;
-    if (s < s1 && task(s, wrow, byte0)) {
-      const int64_t blk = wrow * bpr + byte0 / 32;
+    if (s < s1 && valid_at(s)) {
+      const uint32_t blk = q_base + static_cast<uint32_t>(s - s0) * qk_step;
       q = __ldg(a.qabs + blk);
       a2 = __ldg(a.absmax2 + (blk >> 8));
     } else {
@@ -138,8 +153,7 @@ __global__ void __launch_bounds__(256, 1) nf4_smallm_kernel(const Args a) {
     const int st = static_cast<int>((s - s0) % kStages);
     const int buf = static_cast<int>((s - s0) & 1);
     uint8_t* wt = smem + buf * kWTile;
-    int64_t wrow, byte0;
-    const bool valid = task(s, wrow, byte0);
+    const bool valid = valid_at(s);
     const uint4 w0 = *reinterpret_cast<const uint4*>(smem + kRawOff + st * kRawTile + tid * 32);
     const uint4 w1 = *reinterpret_cast<const uint4*>(smem + kRawOff + st * kRawTile + tid * 32 + 16);
     const float scale = valid ? __fadd_rn(__fmul_rn(code2_s[q0], a20), off) : 0.0f;
@@ -227,6 +241,8 @@ inline Plan plan(int64_t red, int64_t width) {
   Plan p{};
   p.col_tiles = (width + kCols - 1) / kCols;
   p.steps = (red + kStep - 1) / kStep;
+  // Two CTAs per SM in total (short slices win: parallelism matters more here than
+  // the per-CTA prologue).
   int64_t splits = (2 * device_sm_count() + p.col_tiles - 1) / p.col_tiles;
   if (splits > p.steps) splits = p.steps;
   if (splits < 1) splits = 1;
