@@ -7,6 +7,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "gemm_pair.cuh"
 #include "gemm_sm100.cuh"
 
 namespace sb {
@@ -121,8 +122,102 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
   return check_launch(name);
 }
 
+// ----------------------------------------------------------------- 2-SM pair launch
+constexpr int kPairStages = 6;
+
+template <int BMODE, int EMODE, int STAGES>
+inline int configure_pair(const char* name) {
+  using C = pair::PairCfg<BMODE, STAGES>;
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(pair::pair_kernel<BMODE, EMODE, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " smem attribute: " + cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  return SB_OK;
+}
+
+template <int BMODE, int EMODE, int STAGES>
+inline cudaLaunchConfig_t pair_config(int grid, cudaStream_t stream, cudaLaunchAttribute* attr) {
+  using C = pair::PairCfg<BMODE, STAGES>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// CTA pairs that can be resident at once on the current device (74 on a full
+// B200: one pair per TPC), queried once per device.
+inline int pair_slots() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return device_sm_count() / 2;
+  static std::mutex mu;
+  static int cached[64] = {0};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] > 0) return cached[dev];
+  }
+  int n = 0;
+  if (configure_pair<kNF4Fwd, kStoreF16, kPairStages>("nf4_pair_fwd") == SB_OK) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pair_config<kNF4Fwd, kStoreF16, kPairStages>(2, nullptr, attr);
+    if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairStages>, &cfg) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+  }
+  if (n <= 0) n = device_sm_count() / 2;
+  std::lock_guard<std::mutex> lock(mu);
+  cached[dev] = n;
+  return n;
+}
+
+template <int BMODE, int EMODE, int STAGES>
+int launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
+                Params p, int grid, cudaStream_t stream, const char* name) {
+  if (int rc = configure_pair<BMODE, EMODE, STAGES>(name)) return rc;
+  if (grid <= 0) return SB_OK;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pair_config<BMODE, EMODE, STAGES>(grid, stream, attr);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::pair_kernel<BMODE, EMODE, STAGES>, a, b, la, lb, p);
+  if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " launch: " + cudaGetErrorString(e));
+  count_launch();
+  return check_launch(name);
+}
+
 // ----------------------------------------------------------------- NF4 linear
 constexpr int kNF4Msub = 2, kNF4BN = 128, kNF4Stages = 4;
+
+// Kernel choice for the NF4 linear: SB_PAIR=1 forces the 2-SM pair kernel, 0 the
+// one-SM kernel; unset or "auto" applies the size rule below.  Read per call so
+// the workspace query and the launch of one configuration agree.
+inline int pair_override() {
+  const char* e = std::getenv("SB_PAIR");
+  if (!e || !*e || std::string(e) == "auto") return -1;
+  return std::string(e) == "0" ? 0 : 1;
+}
+
+inline bool want_pair(int64_t m, int64_t width) {
+  const int o = pair_override();
+  if (o >= 0) return o == 1;
+  (void)m;
+  (void)width;
+  return false;
+}
 
 inline bool nf4_tc_shape_ok(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
   if (m <= 0 || n_out <= 0 || k_in <= 0) return false;
@@ -135,12 +230,30 @@ inline bool nf4_tc_shape_ok(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
 struct NF4Plan {
   int64_t m_tiles, n_tiles, k_blocks;
   bool streamk;
+  bool pair;     // 2-SM pair kernel (256 x 256 tiles over CTA pairs)
+  int grid;      // CTAs (pair kernel; the one-SM launch sizes its own grid)
   size_t workspace;
 };
 
 inline NF4Plan nf4_plan(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
   NF4Plan pl{};
   const int64_t red = dx ? n_out : k_in, width = dx ? k_in : n_out;
+  if (want_pair(m, width)) {
+    pl.pair = true;
+    pl.m_tiles = (m + pair::kTileM - 1) / pair::kTileM;
+    pl.n_tiles = (width + pair::kTileN - 1) / pair::kTileN;
+    pl.k_blocks = (red + 63) / 64;
+    const int slots = pair_slots();
+    const int64_t tiles = pl.m_tiles * pl.n_tiles;
+    pl.streamk = want_streamk(tiles, pl.k_blocks, slots);
+    const int pairs = pl.streamk ? streamk_grid(tiles, pl.k_blocks, slots)
+                                 : static_cast<int>(tiles < slots ? tiles : slots);
+    pl.grid = 2 * pairs;
+    pl.workspace = pl.streamk ? align256(static_cast<size_t>(pl.grid) * 2 * pair::kSlotF4 * sizeof(float4)) +
+                                    align256(static_cast<size_t>(tiles) * 2 * sizeof(int))
+                              : 0;
+    return pl;
+  }
   pl.m_tiles = (m + kNF4Msub * 128 - 1) / (kNF4Msub * 128);
   pl.n_tiles = (width + kNF4BN - 1) / kNF4BN;
   pl.k_blocks = (red + 63) / 64;
@@ -175,9 +288,12 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
   tla = ta;
   tlb = ta;
   if (r > 0) {
-    rc = make_map(&tla, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_a, r, m, r * 2, r, kNF4Msub * 128, lora_swizzle(r));
+    // LoRA boxes: the A rows of one CTA tile and the B rows that CTA holds.
+    const uint32_t la_rows = pl.pair ? kTileRows : kNF4Msub * 128;
+    const uint32_t lb_rows = pl.pair ? pair::kHalfN : kNF4BN;
+    rc = make_map(&tla, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_a, r, m, r * 2, r, la_rows, lora_swizzle(r));
     if (rc) return rc;
-    rc = make_map(&tlb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_b, r, width, r * 2, r, kNF4BN, lora_swizzle(r));
+    rc = make_map(&tlb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_b, r, width, r * 2, r, lb_rows, lora_swizzle(r));
     if (rc) return rc;
   }
   Params p{};
@@ -188,7 +304,14 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
   p.n_tiles = static_cast<int>(pl.n_tiles);
   p.k_blocks = static_cast<int>(pl.k_blocks);
   p.lora_r = r;
-  if (pl.streamk) {
+  if (pl.streamk && pl.pair) {
+    p.streamk = 1;
+    p.partials = static_cast<float*>(workspace);
+    p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
+                                        align256(static_cast<size_t>(pl.grid) * 2 * pair::kSlotF4 * sizeof(float4)));
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(pl.m_tiles * pl.n_tiles) * 2 * sizeof(int), stream);
+    if (e != cudaSuccess) return fail(SB_ECUDA, std::string("counter reset: ") + cudaGetErrorString(e));
+  } else if (pl.streamk) {
     const int sms = device_sm_count();
     p.streamk = 1;
     p.partials = static_cast<float*>(workspace);
@@ -208,6 +331,12 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
   p.out = out;
   p.ldo = width;
   p.bias = reinterpret_cast<const __half*>(bias);
+  if (pl.pair) {
+    if (!dx) {
+      return launch_pair<kNF4Fwd, kStoreF16, kPairStages>(ta, tb, tla, tlb, p, pl.grid, stream, "nf4_pair_fwd");
+    }
+    return launch_pair<kNF4Dx, kStoreF16, kPairStages>(ta, tb, tla, tlb, p, pl.grid, stream, "nf4_pair_dx");
+  }
   if (!dx) {
     return launch<kNF4Fwd, kStoreF16, kNF4Msub, kNF4BN, kNF4Stages>(ta, tb, tla, tlb, p, stream, "nf4_gemm_fwd");
   }

@@ -1,0 +1,560 @@
+// Two-SM (cta_group::2) NF4 GEMM for sm_100a: one UMMA spans a CTA pair.
+//
+//   D[M, N] = A[M, K] . deq(W)^T (+ LA . LB^T) (+ bias)     fp16 x fp16 -> fp32 (TMEM) -> fp16
+//
+// A cluster of two CTAs (ranks 0 and 1, on the two SMs of one TPC) owns a
+// 256 x 256 output tile.  Each CTA holds its own 128 rows of A and decodes its
+// own 128 rows of B (output columns n0 + 128 * rank ...) into shared memory;
+// the rank-0 CTA issues 256 x 256 x 16 UMMAs (tcgen05.mma.cta_group::2) that
+// read both CTAs' operand halves and write each CTA's 128 accumulator rows x
+// 256 columns into that CTA's TMEM.  Per SM this is a 128 x 256 x 16 UMMA per
+// 8 KB of shared-memory operand reads -- twice the work per byte of the
+// 128 x 128 x 16 UMMA of the one-SM kernel -- with half its per-flop A traffic,
+// while the NF4 decode per flop stays that of a 256 x 128 one-SM tile.
+//
+// Per stage and CTA: A 128 x 64 fp16 (16 KB, SW128), decoded B 128 x 64 fp16
+// (16 KB, SW128; K-major for the forward, two MN-major 64-column panels for dX),
+// packed B 4 KB.  Barriers (same offsets in both CTAs):
+//   full[s]      rank 0 only: A bytes of both CTAs (TMA .cta_group::2 loads signal
+//                rank 0's barrier; rank 0's producer expects both halves)
+//   raw_full[s]  each CTA: its packed B bytes (plain TMA)
+//   decoded[s]   rank 0 only: 256 decoder-thread arrivals, 128 from each CTA
+//   empty[s]     each CTA: one arrival from rank 0's UMMA commit (multicast to both)
+//   acc_full[b]  each CTA: one arrival from rank 0's commit (multicast to both)
+//   acc_empty[b] rank 0 only: 256 epilogue-thread arrivals, 128 from each CTA
+// The protocol is the one of the CUDA PTX ISA's cta_group::2 description and of
+// CUTLASS's 2-SM UMMA pipelines (a transform producer in each CTA arriving on
+// the leader's barrier, the leader's commit released to both CTAs).
+//
+// Every mbarrier wait is bounded (common.cuh).  Before exit each role proves the
+// asynchronous work aimed at its CTA has landed (producer: every stage released
+// by the UMMA; rank 0's issuer: both accumulators released by both epilogues),
+// then all threads of the pair meet at a cluster barrier and free TMEM.
+//
+// Reference: the fused NF4 + LoRA forward / input-gradient of
+// solution/kernels/nf4_gemm.py (decode rule solution/kernels/nf4.py:41-59).
+#pragma once
+
+#include "gemm_sm100.cuh"
+
+namespace sb {
+namespace gemm {
+namespace pair {
+
+// ------------------------------------------------------------ cluster PTX wrappers
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the object at shared::cta address `saddr` in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// All threads of both CTAs (warp-converged).
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier by its shared::cluster address (this CTA's or the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait (as mbar_wait) with cluster-scope acquire, for barriers that
+// receive arrivals from the peer CTA's threads.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int err, volatile int* abort) {
+  const uint32_t addr = smem_addr(bar);
+  if (mbar_try_wait_cluster(addr, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(addr, parity)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - start > kWaitNanos) {
+      atomicOr(&g_device_error, err);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// 2-D tiled load into this CTA's shared memory whose byte count completes on the
+// rank-0 CTA's mbarrier `leader_bar` (a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t leader_bar,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at the same offset in both CTAs once this thread's UMMAs complete.
+__device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
+  const uint16_t mask = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_addr(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+// Same, arriving on this CTA's barrier only.
+__device__ __forceinline__ void umma_commit_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+// Issued by the same warp of both CTAs with the same destination offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ------------------------------------------------------------ configuration
+constexpr int kHalfN = 128;   // B rows (output columns) each CTA decodes per tile
+constexpr int kTileN = 256;   // output columns per pair tile
+constexpr int kTileM = 256;   // output rows per pair tile (128 per CTA)
+
+template <int BMODE, int STAGES>
+struct PairCfg {
+  static constexpr bool kBMN = (BMODE == kNF4Dx);
+  static constexpr int kABytes = kTileRows * kBK * 2;      // 16 KB
+  static constexpr int kBBytes = kHalfN * kBK * 2;         // 16 KB
+  static constexpr int kRawBytes = kHalfN * kBK / 2;       // 4 KB
+  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+  static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
+  static constexpr int kThreads = 512;
+  static constexpr int kBarrierBytes = 1024 + 1024;        // barriers + the code2 table
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 1024;
+  static_assert(STAGES % 2 == 0, "two decoder groups alternate stages: each stage keeps one group");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(kSmemBytes > 232448 / 2, "one CTA per SM keeps TMEM allocation uncontended");
+  static_assert(BMODE == kNF4Fwd || BMODE == kNF4Dx, "NF4 operand modes only");
+};
+
+// Stream-K partial slot of one CTA: [chunk 8][float4 8][thread 128], 128 KB.
+constexpr int kSlotF4 = (kTileN / 32) * 8 * 128;
+
+// ------------------------------------------------------------ epilogue role
+// Warps 4..7 of each CTA: rows m0 + 128 * rank + 32 * (warp % 4) + lane, all 256
+// columns of the tile.  Releases go to rank 0's acc_empty.
+template <int EMODE>
+__device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_base, uint64_t* acc_full,
+                                              uint32_t leader_acc_empty, uint64_t* epi_mb,
+                                              volatile int* abort_flag, volatile int* last_flag, int warp,
+                                              int lane, int num_tiles, int rows_valid, int pair_id, int pairs,
+                                              uint32_t rank) {
+  const int q = warp & 3;
+  const int etid = (warp - 4) * 32 + lane;
+  const int64_t total = static_cast<int64_t>(num_tiles) * p.k_blocks;
+  uint32_t tl = 0, epi_phase = 0;
+  int uidx = 0;
+  UnitIter iter(p, num_tiles, pair_id, pairs);
+  Unit u;
+  while (iter.next(u)) {
+    const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
+    const int m0 = mt * kTileM, n0 = nt * kTileN;
+    if (m0 >= rows_valid) continue;
+    const int buf = tl & 1;
+    const uint32_t aph = (tl >> 1) & 1;
+    if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) break;
+    tc_fence_after();
+    const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kTileN;
+    const int row = m0 + static_cast<int>(rank) * kTileRows + q * 32 + lane;
+    if (u.k0 == 0 && u.k1 == p.k_blocks) {
+      EpiState st;
+      epilogue_begin<EMODE>(p, st, row, rows_valid);
+#pragma unroll 1
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tacc + c * 32, v);
+        tmem_ld_wait();
+        epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+      }
+      epilogue_end<EMODE>(p, st, row, nt, rows_valid);
+      tc_fence_before();
+      mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+    } else {
+      // Stream-K partial tile: park this CTA's 128 x 256 fp32 half in its slot,
+      // release TMEM, and let the last contributing pair to arrive (per half,
+      // counter tile * 2 + rank) sum all slots in pair order and run the epilogue.
+      const int slot = uidx == 0 ? 0 : 1;
+      const int cta = pair_id * 2 + static_cast<int>(rank);
+      float4* mine = reinterpret_cast<float4*>(p.partials) + (static_cast<int64_t>(cta) * 2 + slot) * kSlotF4;
+#pragma unroll 1
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tacc + c * 32, v);
+        tmem_ld_wait();
+        float4* dst = mine + (c * 8) * 128 + etid;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          __stcg(dst + j * 128, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                            __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+      __threadfence();
+      if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+      const int64_t it0 = static_cast<int64_t>(u.tile) * p.k_blocks;
+      const int c_lo = sk_owner(it0, total, pairs);
+      const int c_hi = sk_owner(it0 + p.k_blocks - 1, total, pairs);
+      int* counter = p.counters + static_cast<int64_t>(u.tile) * 2 + rank;
+      if (etid == 0) {
+        const int prev = atomicAdd(counter, 1);
+        *last_flag = (prev == c_hi - c_lo) ? 1 : 0;
+      }
+      if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+      const bool last = *last_flag != 0;
+      if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+      if (last) {
+        __threadfence();
+        EpiState st;
+        epilogue_begin<EMODE>(p, st, row, rows_valid);
+#pragma unroll 1
+        for (int c = 0; c < kTileN / 32; ++c) {
+          float sum[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+          const int64_t off = static_cast<int64_t>(c * 8) * 128 + etid;
+          for (int cc = c_lo; cc <= c_hi; cc += 4) {
+            float4 x[4][8];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const int ci = cc + b;
+              if (ci <= c_hi) {
+                const int64_t first_tile = (total * ci / pairs) / p.k_blocks;
+                const int cslot = first_tile == u.tile ? 0 : 1;
+                const float4* src = reinterpret_cast<const float4*>(p.partials) +
+                                    ((static_cast<int64_t>(ci) * 2 + rank) * 2 + cslot) * kSlotF4 + off;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) x[b][j] = __ldcg(src + j * 128);
+              }
+            }
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              if (cc + b <= c_hi) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  sum[4 * j] += x[b][j].x; sum[4 * j + 1] += x[b][j].y;
+                  sum[4 * j + 2] += x[b][j].z; sum[4 * j + 3] += x[b][j].w;
+                }
+              }
+            }
+          }
+          uint32_t v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(sum[j]);
+          epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
+        }
+        epilogue_end<EMODE>(p, st, row, nt, rows_valid);
+        if (etid == 0) *counter = 0;  // ready for the next launch
+      }
+    }
+    ++tl;
+    ++uidx;
+  }
+}
+
+// ------------------------------------------------------------ the kernel
+template <int BMODE, int EMODE, int STAGES>
+__global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
+    pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
+                const Params p) {
+  using C = PairCfg<BMODE, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bar_area = smem + STAGES * C::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* raw_full = full + STAGES;
+  uint64_t* decoded = raw_full + STAGES;
+  uint64_t* empty = decoded + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint64_t* epi_mb = drain + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(epi_mb + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* last_flag = abort_flag + 1;
+  float* code2_s = reinterpret_cast<float*>(bar_area + 1024);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+  const bool has_lora = p.lora_r > 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&decoded[s], 2 * 128);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * 128);
+    }
+    mbar_init(drain, 1);
+    mbar_init(epi_mb, 128);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) code2_s[i] = __ldg(p.code2 + i);
+  if (warp == 1) tmem_alloc_pair(tmem_holder, C::kTmemCols);
+  tc_fence_before();
+  // Barrier initialisation and the TMEM address must be visible to both CTAs
+  // before any thread signals the peer.
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int rows_valid = runtime_rows(p);
+  // rank 0's barriers, as shared::cluster addresses (stride 8 bytes per barrier)
+  const uint32_t leader_full = map_to_rank(smem_addr(full), 0);
+  const uint32_t leader_decoded = map_to_rank(smem_addr(decoded), 0);
+  const uint32_t leader_acc_empty = map_to_rank(smem_addr(acc_empty), 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      if (has_lora) {
+        tma_prefetch_desc(&tmLA);
+        tma_prefetch_desc(&tmLB);
+      }
+      uint32_t it = 0;
+      bool ok = true;
+      UnitIter iter(p, num_tiles, pair_id, pairs);
+      Unit u;
+      while (ok && iter.next(u)) {
+        const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
+        const int m0 = mt * kTileM;
+        if (m0 >= rows_valid) continue;
+        const int arow = m0 + static_cast<int>(rank) * kTileRows;
+        const int brow = nt * kTileN + static_cast<int>(rank) * kHalfN;
+        const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
+        for (int ls = 0; ls < nsteps; ++ls, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) { ok = false; break; }
+          uint8_t* a_s = smem + s * C::kStageBytes;
+          uint8_t* b_s = a_s + C::kABytes;
+          uint8_t* raw_s = b_s + C::kBBytes;
+          const int step = u.k0 + ls;
+          if (step < u.k1) {
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kABytes);
+            tma_load_2d_pair(a_s, &tmA, leader_full + 8u * s, step * kBK, arow);
+            mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
+            if constexpr (BMODE == kNF4Fwd) {
+              tma_load_2d(raw_s, &tmB, &raw_full[s], step * (kBK / 2), brow);
+            } else {
+              tma_load_2d(raw_s, &tmB, &raw_full[s], brow / 2, step * kBK);
+            }
+          } else {
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * (kTileRows + kHalfN) * p.lora_r * 2);
+            tma_load_2d_pair(a_s, &tmLA, leader_full + 8u * s, 0, arow);
+            tma_load_2d_pair(b_s, &tmLB, leader_full + 8u * s, 0, brow);
+            mbar_arrive(&raw_full[s]);  // nothing to decode: let the decoder group pass
+          }
+        }
+      }
+      // Tail: every stage filled above must be released by the UMMA (which also
+      // shows its bytes landed and the peer's commits arrived) before exit.  After
+      // an abort, wait (bounded once in total) for this CTA's own loads instead.
+      volatile int drain_abort = 0;
+      bool clean = ok && !*abort_flag;
+      for (uint32_t j = it; clean && j < it + STAGES; ++j) {
+        clean = mbar_wait(&empty[j % STAGES], ((j / STAGES) & 1) ^ 1, kErrWaitDrain, abort_flag);
+      }
+      if (!clean) {
+        const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0;
+        for (uint32_t j = first; j < it; ++j) {
+          mbar_wait(&raw_full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
+          if (leader) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer (rank 0)
+    if (lane == 0 && leader) {
+      constexpr uint32_t kIdesc = idesc_f16_f32(kTileM, kTileN, 0, C::kBMN ? 1 : 0);
+      constexpr uint32_t kIdescLora = idesc_f16_f32(kTileM, kTileN, 0, 0);
+      const uint32_t lora_layout = p.lora_r == 16 ? kSwizzle32B : (p.lora_r == 32 ? kSwizzle64B : kSwizzle128B);
+      const uint32_t lora_pitch = static_cast<uint32_t>(p.lora_r) * 2;
+      uint32_t it = 0, tl = 0;
+      bool ok = true;
+      UnitIter iter(p, num_tiles, pair_id, pairs);
+      Unit u;
+      while (ok && iter.next(u)) {
+        if ((u.tile % p.m_tiles) * kTileM >= rows_valid) continue;
+        const int buf = tl & 1;
+        const uint32_t aph = (tl >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + buf * kTileN;
+        const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
+        for (int ls = 0; ls < nsteps; ++ls, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          const bool main_step = u.k0 + ls < u.k1;
+          if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_cluster(&decoded[s], ph, kErrWaitDecoded, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(smem + s * C::kStageBytes);
+          const uint32_t b_addr = a_addr + C::kABytes;
+          if (main_step) {
+#pragma unroll
+            for (int k16 = 0; k16 < kBK / 16; ++k16) {
+              const uint64_t bdesc = C::kBMN
+                  ? smem_desc(b_addr + k16 * 16 * 128, 64 * 128, 1024, kSwizzle128B)
+                  : smem_desc(b_addr + k16 * 32, 16, 1024, kSwizzle128B);
+              const uint64_t adesc = smem_desc(a_addr + k16 * 32, 16, 1024, kSwizzle128B);
+              umma_f16_pair(acc, adesc, bdesc, kIdesc, (ls > 0 || k16 > 0) ? 1u : 0u);
+            }
+          } else {
+            for (int k16 = 0; k16 < p.lora_r / 16; ++k16) {
+              const uint64_t bdesc = smem_desc(b_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
+              const uint64_t adesc = smem_desc(a_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
+              umma_f16_pair(acc, adesc, bdesc, kIdescLora, 1u);
+            }
+          }
+          umma_commit_both(&empty[s]);
+        }
+        if (ok) umma_commit_both(&acc_full[buf]);
+        ++tl;
+      }
+      // Tail: both accumulators released by both CTAs' epilogues (so their last
+      // arrivals on this CTA's acc_empty have landed), then every UMMA complete.
+      if (ok && !*abort_flag) {
+        if (mbar_wait_cluster(&acc_empty[tl & 1], ((tl >> 1) & 1) ^ 1, kErrWaitDrain, abort_flag)) {
+          mbar_wait_cluster(&acc_empty[(tl + 1) & 1], (((tl + 1) >> 1) & 1) ^ 1, kErrWaitDrain, abort_flag);
+        }
+      }
+      umma_commit_local(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, kErrWaitDrain, &no_abort);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    pair_epilogue<EMODE>(p, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
+                         num_tiles, rows_valid, pair_id, pairs, rank);
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ NF4 decoders (both CTAs)
+    // Group g decodes the k-steps whose running index has parity g; thread gtid
+    // decodes one (row, 64-block) of this CTA's 128-row half per step and
+    // arrives on rank 0's decoded barrier.
+    const int group = (warp - 8) >> 2;
+    const int gtid = ((warp - 8) & 3) * 32 + lane;
+    const float off = __ldg(p.offset);
+    const int64_t bpr = p.w_cols / 64;
+    uint32_t it = 0;
+    bool ok = true;
+    auto block_of = [&](int n0, int step) -> int64_t {
+      if constexpr (BMODE == kNF4Fwd) {
+        const int64_t wrow = n0 + gtid;
+        return wrow < p.w_rows ? wrow * bpr + step : -1;
+      } else {
+        const int64_t wrow = static_cast<int64_t>(step) * kBK + (gtid >> 1);
+        const int64_t wcol = n0 + 64 * (gtid & 1);
+        return (wrow < p.w_rows && wcol < p.w_cols) ? wrow * bpr + wcol / 64 : -1;
+      }
+    };
+    UnitIter iter(p, num_tiles, pair_id, pairs);
+    Unit u;
+    while (ok && iter.next(u)) {
+      if ((u.tile % p.m_tiles) * kTileM >= rows_valid) continue;
+      const int n0 = (u.tile / p.m_tiles) * kTileN + static_cast<int>(rank) * kHalfN;
+      const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
+      const int first = u.k0 + ((static_cast<int>(it & 1) == group) ? 0 : 1);
+      int64_t nb = first < u.k1 ? block_of(n0, first) : -1;
+      uint32_t q_next = nb >= 0 ? __ldg(p.qabs + nb) : 0u;
+      float a2_next = nb >= 0 ? __ldg(p.absmax2 + (nb >> 8)) : 0.0f;
+      for (int ls = 0; ls < nsteps; ++ls, ++it) {
+        if (static_cast<int>(it & 1) != group) continue;
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        const int step = u.k0 + ls;
+        const bool main_step = step < u.k1;
+        const uint32_t q_cur = q_next;
+        const float a2_cur = a2_next;
+        const bool valid = main_step && block_of(n0, step) >= 0;
+        nb = step + 2 < u.k1 ? block_of(n0, step + 2) : -1;
+        q_next = nb >= 0 ? __ldg(p.qabs + nb) : 0u;
+        a2_next = nb >= 0 ? __ldg(p.absmax2 + (nb >> 8)) : 0.0f;
+        if (!mbar_wait(&raw_full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
+        if (main_step) {
+          uint8_t* b_s = smem + s * C::kStageBytes + C::kABytes;
+          const uint8_t* raw_s = b_s + C::kBBytes;
+          const float scale = valid ? __fadd_rn(__fmul_rn(code2_s[q_cur], a2_cur), off) : 0.0f;
+          if constexpr (BMODE == kNF4Fwd) {
+            // Raw rows are 32 B, TMA-swizzled in 32 B spans: chunk ^= (row >> 2) & 1.
+            const int r = gtid;
+            const uint32_t x = static_cast<uint32_t>((r >> 2) & 1);
+            nf4_decode_row(raw_s + r * 32 + (x << 4), raw_s + r * 32 + ((x ^ 1u) << 4), b_s + r * 128, r,
+                           scale, valid);
+          } else {
+            // Raw rows are 64 B, TMA-swizzled in 64 B spans: chunk ^= (row >> 1) & 3.
+            const int r = gtid >> 1, j = gtid & 1;
+            const uint32_t x = static_cast<uint32_t>((r >> 1) & 3);
+            const uint8_t* rowp = raw_s + r * 64;
+            nf4_decode_row(rowp + (((2u * j) ^ x) << 4), rowp + (((2u * j + 1u) ^ x) << 4),
+                           b_s + j * (kBK * 128) + r * 128, r, scale, valid);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive_cluster(leader_decoded + 8u * s);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace pair
+}  // namespace gemm
+}  // namespace sb

@@ -352,18 +352,20 @@ struct UnitIter {
   int64_t cursor, end;
   int kb, stride;
   bool streamk;
-  __device__ UnitIter(const Params& p, int num_tiles) {
+  __device__ UnitIter(const Params& p, int num_tiles) : UnitIter(p, num_tiles, blockIdx.x, gridDim.x) {}
+  // Worker `id` of `count` (a CTA, or a CTA pair of a 2-SM kernel).
+  __device__ UnitIter(const Params& p, int num_tiles, int id, int count) {
     streamk = p.streamk != 0;
     kb = p.k_blocks;
     if (streamk) {
       const int64_t total = static_cast<int64_t>(num_tiles) * kb;
-      cursor = total * blockIdx.x / gridDim.x;
-      end = total * (blockIdx.x + 1) / gridDim.x;
+      cursor = total * id / count;
+      end = total * (id + 1) / count;
       stride = 0;
     } else {
-      cursor = blockIdx.x;
+      cursor = id;
       end = num_tiles;
-      stride = gridDim.x;
+      stride = count;
     }
   }
   __device__ bool next(Unit& u) {
