@@ -125,7 +125,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
 // ----------------------------------------------------------------- 2-SM pair launch
 constexpr int kPairStages = 6;
 
-template <int BMODE, int EMODE, int STAGES>
+template <int BMODE, int EMODE, int STAGES, bool SK>
 inline int configure_pair(const char* name) {
   using C = pair::PairCfg<BMODE, STAGES>;
   static std::mutex mu;
@@ -134,7 +134,7 @@ inline int configure_pair(const char* name) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(pair::pair_kernel<BMODE, EMODE, STAGES>,
+    cudaError_t e = cudaFuncSetAttribute(pair::pair_kernel<BMODE, EMODE, STAGES, SK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " smem attribute: " + cudaGetErrorString(e));
     configured[dev] = true;
@@ -171,10 +171,10 @@ inline int pair_slots() {
     if (cached[dev] > 0) return cached[dev];
   }
   int n = 0;
-  if (configure_pair<kNF4Fwd, kStoreF16, kPairStages>("nf4_pair_fwd") == SB_OK) {
+  if (configure_pair<kNF4Fwd, kStoreF16, kPairStages, false>("nf4_pair_fwd") == SB_OK) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pair_config<kNF4Fwd, kStoreF16, kPairStages>(2, nullptr, attr);
-    if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairStages>, &cfg) !=
+    if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairStages, false>, &cfg) !=
         cudaSuccess) {
       cudaGetLastError();
       n = 0;
@@ -186,17 +186,24 @@ inline int pair_slots() {
   return n;
 }
 
-template <int BMODE, int EMODE, int STAGES>
-int launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
-                Params p, int grid, cudaStream_t stream, const char* name) {
-  if (int rc = configure_pair<BMODE, EMODE, STAGES>(name)) return rc;
+template <int BMODE, int EMODE, int STAGES, bool SK>
+int launch_pair_sk(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
+                   const CUtensorMap& y, Params p, int grid, cudaStream_t stream, const char* name) {
+  if (int rc = configure_pair<BMODE, EMODE, STAGES, SK>(name)) return rc;
   if (grid <= 0) return SB_OK;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pair_config<BMODE, EMODE, STAGES>(grid, stream, attr);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::pair_kernel<BMODE, EMODE, STAGES>, a, b, la, lb, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::pair_kernel<BMODE, EMODE, STAGES, SK>, a, b, la, lb, y, p);
   if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " launch: " + cudaGetErrorString(e));
   count_launch();
   return check_launch(name);
+}
+
+template <int BMODE, int EMODE, int STAGES>
+int launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
+                const CUtensorMap& y, Params p, int grid, cudaStream_t stream, const char* name) {
+  return p.streamk ? launch_pair_sk<BMODE, EMODE, STAGES, true>(a, b, la, lb, y, p, grid, stream, name)
+                   : launch_pair_sk<BMODE, EMODE, STAGES, false>(a, b, la, lb, y, p, grid, stream, name);
 }
 
 // ----------------------------------------------------------------- NF4 linear
@@ -322,6 +329,7 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
     if (e != cudaSuccess) return fail(SB_ECUDA, std::string("counter reset: ") + cudaGetErrorString(e));
   }
   p.vec_ok = aligned(out, 16) && (width % 8 == 0);
+  p.packed = w.packed;
   p.qabs = w.qabs;
   p.absmax2 = w.absmax2;
   p.code2 = w.code2;
@@ -332,10 +340,19 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
   p.ldo = width;
   p.bias = reinterpret_cast<const __half*>(bias);
   if (pl.pair) {
-    if (!dx) {
-      return launch_pair<kNF4Fwd, kStoreF16, kPairStages>(ta, tb, tla, tlb, p, pl.grid, stream, "nf4_pair_fwd");
+    // Output tensor map for the bulk-store epilogue: box 64 columns x 32 rows (one
+    // epilogue warp's rows), 128B swizzle; needs 16-byte aligned rows.
+    CUtensorMap ty = ta;
+    p.store_tma = (aligned(out, 16) && width % 8 == 0) ? 1 : 0;
+    if (p.store_tma) {
+      rc = make_map(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out, width, m, width * 2, 64, 32,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
     }
-    return launch_pair<kNF4Dx, kStoreF16, kPairStages>(ta, tb, tla, tlb, p, pl.grid, stream, "nf4_pair_dx");
+    if (!dx) {
+      return launch_pair<kNF4Fwd, kStoreF16, kPairStages>(ta, tb, tla, tlb, ty, p, pl.grid, stream, "nf4_pair_fwd");
+    }
+    return launch_pair<kNF4Dx, kStoreF16, kPairStages>(ta, tb, tla, tlb, ty, p, pl.grid, stream, "nf4_pair_dx");
   }
   if (!dx) {
     return launch<kNF4Fwd, kStoreF16, kNF4Msub, kNF4BN, kNF4Stages>(ta, tb, tla, tlb, p, stream, "nf4_gemm_fwd");

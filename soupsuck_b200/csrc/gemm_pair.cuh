@@ -12,14 +12,18 @@
 // 128 x 128 x 16 UMMA of the one-SM kernel -- with half its per-flop A traffic,
 // while the NF4 decode per flop stays that of a 256 x 128 one-SM tile.
 //
-// Per stage and CTA: A 128 x 64 fp16 (16 KB, SW128), decoded B 128 x 64 fp16
-// (16 KB, SW128; K-major for the forward, two MN-major 64-column panels for dX),
-// packed B 4 KB.  Barriers (same offsets in both CTAs):
+// Per stage and CTA: A 128 x 64 fp16 (16 KB, SW128) and decoded B 128 x 64 fp16
+// (16 KB, SW128; K-major for the forward, two MN-major 64-column panels for dX).
+// The decoders load their packed bytes straight from global memory into
+// registers one owned step ahead: shared-memory bandwidth (128 B/cycle/SM) is
+// the binding resource of this kernel -- per k-step the UMMAs read 32 KB, the A
+// TMA writes 16 KB and the decoders write 16 KB -- so packed bytes are kept out
+// of shared memory.  Barriers (same offsets in both CTAs):
 //   full[s]      rank 0 only: A bytes of both CTAs (TMA .cta_group::2 loads signal
 //                rank 0's barrier; rank 0's producer expects both halves)
-//   raw_full[s]  each CTA: its packed B bytes (plain TMA)
 //   decoded[s]   rank 0 only: 256 decoder-thread arrivals, 128 from each CTA
-//   empty[s]     each CTA: one arrival from rank 0's UMMA commit (multicast to both)
+//   empty[s]     each CTA: one arrival from rank 0's UMMA commit (multicast to both);
+//                waited on by the producer (A slot) and the decoders (B slot)
 //   acc_full[b]  each CTA: one arrival from rank 0's commit (multicast to both)
 //   acc_empty[b] rank 0 only: 256 epilogue-thread arrivals, 128 from each CTA
 // The protocol is the one of the CUDA PTX ISA's cta_group::2 description and of
@@ -61,39 +65,37 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive on an mbarrier by its shared::cluster address (this CTA's or the peer's).
+// Arrive on an mbarrier by its shared::cluster address (this CTA's or the peer's),
+// with the instruction's default semantics.  A cluster-scope release here would
+// be a fence that waits for the thread's outstanding global loads (the decoders'
+// scale prefetch), measured as membar stalls; the arrivals ordered by it are
+// shared-memory writes made visible to the tensor core by fence.proxy.async.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return ok != 0;
+// 16-byte read-only global load that does not allocate in L1 (L1 shares the
+// SRAM and data pipe with shared memory).
+__device__ __forceinline__ uint4 ld_stream16(const uint4* ptr) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr));
+  return v;
 }
 
-// Bounded wait (as mbar_wait) with cluster-scope acquire, for barriers that
-// receive arrivals from the peer CTA's threads.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int err, volatile int* abort) {
-  const uint32_t addr = smem_addr(bar);
-  if (mbar_try_wait_cluster(addr, parity)) return true;
-  const uint64_t start = global_timer_ns();
-  while (true) {
-    if (mbar_try_wait_cluster(addr, parity)) return true;
-    if (*abort) return false;
-    if (global_timer_ns() - start > kWaitNanos) {
-      atomicOr(&g_device_error, err);
-      *abort = 1;
-      return false;
-    }
-  }
+// Bulk tensor store of a shared-memory box to global memory (out-of-range rows and
+// columns of the box are clipped by the tensor map), tracked by bulk groups.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y)
+               : "memory");
 }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most one committed store group still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // 2-D tiled load into this CTA's shared memory whose byte count completes on the
 // rank-0 CTA's mbarrier `leader_bar` (a shared::cluster address).  No multicast.
@@ -106,31 +108,45 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
-__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                              uint32_t idesc, uint32_t accumulate) {
+// Converged-warp forms: the whole warp executes them with warp-uniform operands
+// and elect.sync picks the single lane that issues.  An issue loop run by one
+// lane of a diverged warp measured ~100 cycles per tcgen05 instruction.
+__device__ __forceinline__ void umma_f16_pair_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                   uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// Arrive on the barrier at the same offset in both CTAs once this thread's UMMAs complete.
-__device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
+__device__ __forceinline__ void umma_commit_both_warp(uint64_t* bar) {
   const uint16_t mask = 3;
   asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
           smem_addr(bar)),
       "h"(mask)
       : "memory");
 }
 
-// Same, arriving on this CTA's barrier only.
-__device__ __forceinline__ void umma_commit_local(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_addr(bar))
-               : "memory");
+__device__ __forceinline__ void umma_commit_local_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar))
+      : "memory");
+}
+
+// Bounded wait by lane 0 of a converged warp; the outcome is broadcast so the
+// warp's control flow stays uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int err, volatile int* abort, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait(bar, parity, err, abort) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
 // Issued by the same warp of both CTAs with the same destination offset.
@@ -154,12 +170,14 @@ struct PairCfg {
   static constexpr bool kBMN = (BMODE == kNF4Dx);
   static constexpr int kABytes = kTileRows * kBK * 2;      // 16 KB
   static constexpr int kBBytes = kHalfN * kBK * 2;         // 16 KB
-  static constexpr int kRawBytes = kHalfN * kBK / 2;       // 4 KB
-  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
   static constexpr int kThreads = 512;
   static constexpr int kBarrierBytes = 1024 + 1024;        // barriers + the code2 table
-  static constexpr int kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 1024;
+  // Epilogue staging: per epilogue warp two 32-row x 64-column fp16 boxes (SW128).
+  static constexpr int kStoreBoxBytes = 32 * 64 * 2;
+  static constexpr int kStagingBytes = 4 * 2 * kStoreBoxBytes;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + kBarrierBytes + 1024;
   static_assert(STAGES % 2 == 0, "two decoder groups alternate stages: each stage keeps one group");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kSmemBytes > 232448 / 2, "one CTA per SM keeps TMEM allocation uncontended");
@@ -172,8 +190,9 @@ constexpr int kSlotF4 = (kTileN / 32) * 8 * 128;
 // ------------------------------------------------------------ epilogue role
 // Warps 4..7 of each CTA: rows m0 + 128 * rank + 32 * (warp % 4) + lane, all 256
 // columns of the tile.  Releases go to rank 0's acc_empty.
-template <int EMODE>
-__device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_base, uint64_t* acc_full,
+template <int EMODE, bool SK>
+__device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap* tmY, uint8_t* staging,
+                                              uint32_t tmem_base, uint64_t* acc_full,
                                               uint32_t leader_acc_empty, uint64_t* epi_mb,
                                               volatile int* abort_flag, volatile int* last_flag, int warp,
                                               int lane, int num_tiles, int rows_valid, int pair_id, int pairs,
@@ -181,8 +200,10 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_bas
   const int q = warp & 3;
   const int etid = (warp - 4) * 32 + lane;
   const int64_t total = static_cast<int64_t>(num_tiles) * p.k_blocks;
-  uint32_t tl = 0, epi_phase = 0;
+  uint32_t tl = 0, epi_phase = 0, boxes = 0;
   int uidx = 0;
+  // This warp's two staging boxes; rows of a box are this warp's 32 TMEM lanes.
+  uint8_t* my_boxes = staging + (warp - 4) * 2 * (32 * 64 * 2);
   UnitIter iter(p, num_tiles, pair_id, pairs);
   Unit u;
   while (iter.next(u)) {
@@ -195,7 +216,53 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_bas
     tc_fence_after();
     const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kTileN;
     const int row = m0 + static_cast<int>(rank) * kTileRows + q * 32 + lane;
-    if (u.k0 == 0 && u.k1 == p.k_blocks) {
+    if ((!SK || (u.k0 == 0 && u.k1 == p.k_blocks)) && p.store_tma) {
+      // fp32 (+ bias) -> fp16, staged per 64-column panel into a 128B-swizzled box
+      // and written by one bulk tensor store: every global write is a full
+      // 128-byte row segment instead of 32 scattered 16-byte pieces per warp store.
+      const int row0 = m0 + static_cast<int>(rank) * kTileRows + q * 32;
+#pragma unroll 1
+      for (int panel = 0; panel < kTileN / 64; ++panel) {
+        // The store issued from this box two panels ago must have finished reading it.
+        if (lane == 0) bulk_wait_read1();
+        __syncwarp();
+        uint8_t* box = my_boxes + (boxes & 1) * (32 * 64 * 2);
+        const uint32_t swz = static_cast<uint32_t>(lane & 7);
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t v[32];
+          tmem_ld32(tacc + panel * 64 + half * 32, v);
+          tmem_ld_wait();
+          const int col0 = n0 + panel * 64 + half * 32;
+          uint32_t h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float f0 = __uint_as_float(v[2 * j]), f1 = __uint_as_float(v[2 * j + 1]);
+            if (p.bias) {
+              if (col0 + 2 * j < p.N) f0 = __fadd_rn(f0, __half2float(p.bias[col0 + 2 * j]));
+              if (col0 + 2 * j + 1 < p.N) f1 = __fadd_rn(f1, __half2float(p.bias[col0 + 2 * j + 1]));
+            }
+            __half2 t = __floats2half2_rn(f0, f1);
+            h[j] = *reinterpret_cast<uint32_t*>(&t);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t unit = static_cast<uint32_t>(half * 4 + c);
+            *reinterpret_cast<uint4*>(box + lane * 128 + ((unit ^ swz) << 4)) =
+                make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmY, box, n0 + panel * 64, row0);
+          bulk_commit();
+        }
+        ++boxes;
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+    } else if (!SK || (u.k0 == 0 && u.k1 == p.k_blocks)) {
       EpiState st;
       epilogue_begin<EMODE>(p, st, row, rows_valid);
 #pragma unroll 1
@@ -208,7 +275,7 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_bas
       epilogue_end<EMODE>(p, st, row, nt, rows_valid);
       tc_fence_before();
       mbar_arrive_cluster(leader_acc_empty + 8u * buf);
-    } else {
+    } else if constexpr (SK) {
       // Stream-K partial tile: park this CTA's 128 x 256 fp32 half in its slot,
       // release TMEM, and let the last contributing pair to arrive (per half,
       // counter tile * 2 + rank) sum all slots in pair order and run the epilogue.
@@ -252,10 +319,10 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_bas
 #pragma unroll
           for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
           const int64_t off = static_cast<int64_t>(c * 8) * 128 + etid;
-          for (int cc = c_lo; cc <= c_hi; cc += 4) {
-            float4 x[4][8];
+          for (int cc = c_lo; cc <= c_hi; cc += 2) {
+            float4 x[2][8];
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
+            for (int b = 0; b < 2; ++b) {
               const int ci = cc + b;
               if (ci <= c_hi) {
                 const int64_t first_tile = (total * ci / pairs) / p.k_blocks;
@@ -267,7 +334,7 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_bas
               }
             }
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
+            for (int b = 0; b < 2; ++b) {
               if (cc + b <= c_hi) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -289,21 +356,26 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, uint32_t tmem_bas
     ++tl;
     ++uidx;
   }
+  // Stores must finish reading the staging boxes before the CTA exits.
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
 }
 
 // ------------------------------------------------------------ the kernel
-template <int BMODE, int EMODE, int STAGES>
+// SK: stream-K schedule (partial tiles and their fix-up); the whole-tile
+// instantiation carries no fix-up code, which keeps it free of register spills.
+template <int BMODE, int EMODE, int STAGES, bool SK>
 __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
     pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
-                const Params p) {
+                const __grid_constant__ CUtensorMap tmY, const Params p) {
   using C = PairCfg<BMODE, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bar_area = smem + STAGES * C::kStageBytes;
+  uint8_t* staging = smem + STAGES * C::kStageBytes;
+  uint8_t* bar_area = staging + C::kStagingBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
-  uint64_t* raw_full = full + STAGES;
-  uint64_t* decoded = raw_full + STAGES;
+  uint64_t* decoded = full + STAGES;
   uint64_t* empty = decoded + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -326,7 +398,6 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&raw_full[s], 1);
       mbar_init(&decoded[s], 2 * 128);
       mbar_init(&empty[s], 1);
     }
@@ -357,8 +428,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      tma_prefetch_desc(&tmA);
-      tma_prefetch_desc(&tmB);
+      tma_prefetch_desc(&tmA);  // tmB is unused: the decoders read packed codes directly
       if (has_lora) {
         tma_prefetch_desc(&tmLA);
         tma_prefetch_desc(&tmLB);
@@ -380,44 +450,37 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
           if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) { ok = false; break; }
           uint8_t* a_s = smem + s * C::kStageBytes;
           uint8_t* b_s = a_s + C::kABytes;
-          uint8_t* raw_s = b_s + C::kBBytes;
           const int step = u.k0 + ls;
           if (step < u.k1) {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kABytes);
             tma_load_2d_pair(a_s, &tmA, leader_full + 8u * s, step * kBK, arow);
-            mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
-            if constexpr (BMODE == kNF4Fwd) {
-              tma_load_2d(raw_s, &tmB, &raw_full[s], step * (kBK / 2), brow);
-            } else {
-              tma_load_2d(raw_s, &tmB, &raw_full[s], brow / 2, step * kBK);
-            }
           } else {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * (kTileRows + kHalfN) * p.lora_r * 2);
             tma_load_2d_pair(a_s, &tmLA, leader_full + 8u * s, 0, arow);
             tma_load_2d_pair(b_s, &tmLB, leader_full + 8u * s, 0, brow);
-            mbar_arrive(&raw_full[s]);  // nothing to decode: let the decoder group pass
           }
         }
       }
       // Tail: every stage filled above must be released by the UMMA (which also
       // shows its bytes landed and the peer's commits arrived) before exit.  After
-      // an abort, wait (bounded once in total) for this CTA's own loads instead.
+      // an abort rank 0 waits (bounded once in total) for the loads on its barriers.
       volatile int drain_abort = 0;
       bool clean = ok && !*abort_flag;
       for (uint32_t j = it; clean && j < it + STAGES; ++j) {
         clean = mbar_wait(&empty[j % STAGES], ((j / STAGES) & 1) ^ 1, kErrWaitDrain, abort_flag);
       }
-      if (!clean) {
+      if (!clean && leader) {
         const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0;
         for (uint32_t j = first; j < it; ++j) {
-          mbar_wait(&raw_full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
-          if (leader) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
+          mbar_wait(&full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (rank 0)
-    if (lane == 0 && leader) {
+    // The whole warp runs the loop so the descriptors stay warp-uniform; lane 0
+    // waits, one elected lane issues.
+    if (leader) {
       constexpr uint32_t kIdesc = idesc_f16_f32(kTileM, kTileN, 0, C::kBMN ? 1 : 0);
       constexpr uint32_t kIdescLora = idesc_f16_f32(kTileM, kTileN, 0, 0);
       const uint32_t lora_layout = p.lora_r == 16 ? kSwizzle32B : (p.lora_r == 32 ? kSwizzle64B : kSwizzle128B);
@@ -430,7 +493,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
         if ((u.tile % p.m_tiles) * kTileM >= rows_valid) continue;
         const int buf = tl & 1;
         const uint32_t aph = (tl >> 1) & 1;
-        if (!mbar_wait_cluster(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag)) { ok = false; break; }
+        if (!warp_wait(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag, lane)) { ok = false; break; }
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * kTileN;
         const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
@@ -438,8 +501,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           const bool main_step = u.k0 + ls < u.k1;
-          if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
-          if (!mbar_wait_cluster(&decoded[s], ph, kErrWaitDecoded, abort_flag)) { ok = false; break; }
+          if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag, lane)) { ok = false; break; }
+          if (!warp_wait(&decoded[s], ph, kErrWaitDecoded, abort_flag, lane)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + s * C::kStageBytes);
           const uint32_t b_addr = a_addr + C::kABytes;
@@ -450,45 +513,51 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
                   ? smem_desc(b_addr + k16 * 16 * 128, 64 * 128, 1024, kSwizzle128B)
                   : smem_desc(b_addr + k16 * 32, 16, 1024, kSwizzle128B);
               const uint64_t adesc = smem_desc(a_addr + k16 * 32, 16, 1024, kSwizzle128B);
-              umma_f16_pair(acc, adesc, bdesc, kIdesc, (ls > 0 || k16 > 0) ? 1u : 0u);
+              umma_f16_pair_warp(acc, adesc, bdesc, kIdesc, (ls > 0 || k16 > 0) ? 1u : 0u);
             }
           } else {
             for (int k16 = 0; k16 < p.lora_r / 16; ++k16) {
               const uint64_t bdesc = smem_desc(b_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
               const uint64_t adesc = smem_desc(a_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
-              umma_f16_pair(acc, adesc, bdesc, kIdescLora, 1u);
+              umma_f16_pair_warp(acc, adesc, bdesc, kIdescLora, 1u);
             }
           }
-          umma_commit_both(&empty[s]);
+          umma_commit_both_warp(&empty[s]);
         }
-        if (ok) umma_commit_both(&acc_full[buf]);
+        if (ok) umma_commit_both_warp(&acc_full[buf]);
         ++tl;
       }
       // Tail: both accumulators released by both CTAs' epilogues (so their last
       // arrivals on this CTA's acc_empty have landed), then every UMMA complete.
       if (ok && !*abort_flag) {
-        if (mbar_wait_cluster(&acc_empty[tl & 1], ((tl >> 1) & 1) ^ 1, kErrWaitDrain, abort_flag)) {
-          mbar_wait_cluster(&acc_empty[(tl + 1) & 1], (((tl + 1) >> 1) & 1) ^ 1, kErrWaitDrain, abort_flag);
+        if (warp_wait(&acc_empty[tl & 1], ((tl >> 1) & 1) ^ 1, kErrWaitDrain, abort_flag, lane)) {
+          warp_wait(&acc_empty[(tl + 1) & 1], (((tl + 1) >> 1) & 1) ^ 1, kErrWaitDrain, abort_flag, lane);
         }
       }
-      umma_commit_local(drain);
+      umma_commit_local_warp(drain);
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, kErrWaitDrain, &no_abort);
+      warp_wait(drain, 0, kErrWaitDrain, &no_abort, lane);
     }
   } else if (warp >= 4 && warp < 8) {
-    pair_epilogue<EMODE>(p, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
+    if (lane == 0 && p.store_tma) tma_prefetch_desc(&tmY);
+    pair_epilogue<EMODE, SK>(p, &tmY, staging, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
                          num_tiles, rows_valid, pair_id, pairs, rank);
   } else if (warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders (both CTAs)
     // Group g decodes the k-steps whose running index has parity g; thread gtid
     // decodes one (row, 64-block) of this CTA's 128-row half per step and
-    // arrives on rank 0's decoded barrier.
+    // arrives on rank 0's decoded barrier.  The block's 32 packed bytes, its
+    // qabs byte and absmax2 value are loaded for the group's next step while the
+    // current one decodes; the B slot is reused once empty[s] shows the UMMA
+    // that read it has completed.
     const int group = (warp - 8) >> 2;
     const int gtid = ((warp - 8) & 3) * 32 + lane;
     const float off = __ldg(p.offset);
     const int64_t bpr = p.w_cols / 64;
+    const int64_t pitch = p.w_cols / 2;  // packed bytes per weight row
     uint32_t it = 0;
     bool ok = true;
+    // Block index of this thread's (row, 64-block) at k-step `step`, or -1 outside the weight.
     auto block_of = [&](int n0, int step) -> int64_t {
       if constexpr (BMODE == kNF4Fwd) {
         const int64_t wrow = n0 + gtid;
@@ -499,6 +568,14 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
         return (wrow < p.w_rows && wcol < p.w_cols) ? wrow * bpr + wcol / 64 : -1;
       }
     };
+    // Byte offset of that block's packed codes (row-major packing, 32 bytes per block).
+    auto bytes_of = [&](int n0, int step) -> int64_t {
+      if constexpr (BMODE == kNF4Fwd) {
+        return static_cast<int64_t>(n0 + gtid) * pitch + step * (kBK / 2);
+      } else {
+        return (static_cast<int64_t>(step) * kBK + (gtid >> 1)) * pitch + (n0 + 64 * (gtid & 1)) / 2;
+      }
+    };
     UnitIter iter(p, num_tiles, pair_id, pairs);
     Unit u;
     while (ok && iter.next(u)) {
@@ -507,38 +584,43 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
       const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
       const int first = u.k0 + ((static_cast<int>(it & 1) == group) ? 0 : 1);
       int64_t nb = first < u.k1 ? block_of(n0, first) : -1;
-      uint32_t q_next = nb >= 0 ? __ldg(p.qabs + nb) : 0u;
-      float a2_next = nb >= 0 ? __ldg(p.absmax2 + (nb >> 8)) : 0.0f;
+      uint4 w0_next = make_uint4(0, 0, 0, 0), w1_next = make_uint4(0, 0, 0, 0);
+      uint32_t q_next = 0u;
+      float a2_next = 0.0f;
+      if (nb >= 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, first));
+        w0_next = ld_stream16(src);
+        w1_next = ld_stream16(src + 1);
+        q_next = __ldg(p.qabs + nb);
+        a2_next = __ldg(p.absmax2 + (nb >> 8));
+      }
       for (int ls = 0; ls < nsteps; ++ls, ++it) {
         if (static_cast<int>(it & 1) != group) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         const int step = u.k0 + ls;
         const bool main_step = step < u.k1;
+        const uint4 w0 = w0_next, w1 = w1_next;
         const uint32_t q_cur = q_next;
         const float a2_cur = a2_next;
         const bool valid = main_step && block_of(n0, step) >= 0;
         nb = step + 2 < u.k1 ? block_of(n0, step + 2) : -1;
-        q_next = nb >= 0 ? __ldg(p.qabs + nb) : 0u;
-        a2_next = nb >= 0 ? __ldg(p.absmax2 + (nb >> 8)) : 0.0f;
-        if (!mbar_wait(&raw_full[s], ph, kErrWaitFull, abort_flag)) { ok = false; break; }
+        if (nb >= 0) {
+          const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, step + 2));
+          w0_next = ld_stream16(src);
+          w1_next = ld_stream16(src + 1);
+          q_next = __ldg(p.qabs + nb);
+          a2_next = __ldg(p.absmax2 + (nb >> 8));
+        }
+        if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) { ok = false; break; }
         if (main_step) {
           uint8_t* b_s = smem + s * C::kStageBytes + C::kABytes;
-          const uint8_t* raw_s = b_s + C::kBBytes;
           const float scale = valid ? __fadd_rn(__fmul_rn(code2_s[q_cur], a2_cur), off) : 0.0f;
           if constexpr (BMODE == kNF4Fwd) {
-            // Raw rows are 32 B, TMA-swizzled in 32 B spans: chunk ^= (row >> 2) & 1.
-            const int r = gtid;
-            const uint32_t x = static_cast<uint32_t>((r >> 2) & 1);
-            nf4_decode_row(raw_s + r * 32 + (x << 4), raw_s + r * 32 + ((x ^ 1u) << 4), b_s + r * 128, r,
-                           scale, valid);
+            nf4_decode_words(w0, w1, b_s + gtid * 128, gtid, scale, valid);
           } else {
-            // Raw rows are 64 B, TMA-swizzled in 64 B spans: chunk ^= (row >> 1) & 3.
             const int r = gtid >> 1, j = gtid & 1;
-            const uint32_t x = static_cast<uint32_t>((r >> 1) & 3);
-            const uint8_t* rowp = raw_s + r * 64;
-            nf4_decode_row(rowp + (((2u * j) ^ x) << 4), rowp + (((2u * j + 1u) ^ x) << 4),
-                           b_s + j * (kBK * 128) + r * 128, r, scale, valid);
+            nf4_decode_words(w0, w1, b_s + j * (kBK * 128) + r * 128, r, scale, valid);
           }
         }
         fence_proxy_async_smem();

@@ -47,10 +47,12 @@ struct Params {
   int lora_r;             // 0, 16, 32 or 64: extra LoRA step(s) after the main loop
   const int* m_dev;       // optional runtime row count (CE backward compaction)
   int vec_ok;             // output rows are 16-byte aligned
+  int store_tma;          // 2-SM pair kernel: fp16 output written by bulk tensor stores
   int streamk;            // 1: stream-K schedule (equal k-iteration shares per CTA)
   float* partials;        // stream-K: [grid, 2, MSUB*128, BN] fp32 partial tiles
   int* counters;          // stream-K: [tiles] arrival counters, zero before launch
   // NF4 weight
+  const uint8_t* packed;   // packed codes (read directly by the 2-SM pair kernel's decoders)
   const uint8_t* qabs;
   const float* absmax2;
   const float* code2;
