@@ -126,6 +126,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
+// Same, letting the hardware suspend the thread until the phase completes or
+// `hint_ns` elapse: a waiting warp then takes no issue slots from the warps
+// that share its scheduler (a polling loop measurably slowed the UMMA issuer).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Suspension bound of one wait round: the abort flag and the time limit are
+// checked at least this often.
+constexpr uint32_t kSuspendHintNanos = 100000;
+
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // (and records `err`) once kWaitNanos elapse, or at once if `abort` is set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err,
@@ -134,7 +153,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int er
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_wait_suspend(addr, parity, kSuspendHintNanos)) return true;
     if (*abort) return false;
     if (global_timer_ns() - start > kWaitNanos) {
       atomicOr(&g_device_error, err);

@@ -14,16 +14,20 @@
 //
 // Per stage and CTA: A 128 x 64 fp16 (16 KB, SW128) and decoded B 128 x 64 fp16
 // (16 KB, SW128; K-major for the forward, two MN-major 64-column panels for dX).
-// The decoders load their packed bytes straight from global memory into
-// registers one owned step ahead: shared-memory bandwidth (128 B/cycle/SM) is
-// the binding resource of this kernel -- per k-step the UMMAs read 32 KB, the A
-// TMA writes 16 KB and the decoders write 16 KB -- so packed bytes are kept out
-// of shared memory.  Barriers (same offsets in both CTAs):
+// Two measured configurations (B200, Qwen2.5 layer shapes):
+//   forward: the producer also TMA-loads each step's packed codes (4 KB) into the
+//            stage (raw_full[s]); the epilogue stores fp16 rows directly;
+//   dX:      the decoders load their packed codes straight from global memory one
+//            owned step ahead, and the epilogue stages 32 x 64 boxes in shared
+//            memory for bulk tensor stores.
+// Both fit six stages: 6 x 36 KB, or 6 x 32 KB + 32 KB of store staging.
+// Barriers (same offsets in both CTAs):
 //   full[s]      rank 0 only: A bytes of both CTAs (TMA .cta_group::2 loads signal
 //                rank 0's barrier; rank 0's producer expects both halves)
+//   raw_full[s]  forward, each CTA: its packed codes (plain TMA)
 //   decoded[s]   rank 0 only: 256 decoder-thread arrivals, 128 from each CTA
 //   empty[s]     each CTA: one arrival from rank 0's UMMA commit (multicast to both);
-//                waited on by the producer (A slot) and the decoders (B slot)
+//                waited on by the producer and, for dX, the decoders (B slot)
 //   acc_full[b]  each CTA: one arrival from rank 0's commit (multicast to both)
 //   acc_empty[b] rank 0 only: 256 epilogue-thread arrivals, 128 from each CTA
 // The protocol is the one of the CUDA PTX ISA's cta_group::2 description and of
@@ -170,13 +174,16 @@ struct PairCfg {
   static constexpr bool kBMN = (BMODE == kNF4Dx);
   static constexpr int kABytes = kTileRows * kBK * 2;      // 16 KB
   static constexpr int kBBytes = kHalfN * kBK * 2;         // 16 KB
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr bool kRawTma = (BMODE == kNF4Fwd);     // packed codes via TMA + smem
+  static constexpr bool kStoreStage = !kRawTma;            // bulk-store epilogue
+  static constexpr int kRawBytes = kRawTma ? kHalfN * kBK / 2 : 0;   // 4 KB
+  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
   static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
   static constexpr int kThreads = 512;
   static constexpr int kBarrierBytes = 1024 + 1024;        // barriers + the code2 table
   // Epilogue staging: per epilogue warp two 32-row x 64-column fp16 boxes (SW128).
   static constexpr int kStoreBoxBytes = 32 * 64 * 2;
-  static constexpr int kStagingBytes = 4 * 2 * kStoreBoxBytes;
+  static constexpr int kStagingBytes = kStoreStage ? 4 * 2 * kStoreBoxBytes : 0;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + kBarrierBytes + 1024;
   static_assert(STAGES % 2 == 0, "two decoder groups alternate stages: each stage keeps one group");
   static_assert(kSmemBytes <= 232448, "shared memory");
@@ -190,7 +197,8 @@ constexpr int kSlotF4 = (kTileN / 32) * 8 * 128;
 // ------------------------------------------------------------ epilogue role
 // Warps 4..7 of each CTA: rows m0 + 128 * rank + 32 * (warp % 4) + lane, all 256
 // columns of the tile.  Releases go to rank 0's acc_empty.
-template <int EMODE, bool SK>
+// STAGE: the kernel has store staging (bulk-store epilogue available).
+template <int EMODE, bool SK, bool STAGE>
 __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap* tmY, uint8_t* staging,
                                               uint32_t tmem_base, uint64_t* acc_full,
                                               uint32_t leader_acc_empty, uint64_t* epi_mb,
@@ -216,7 +224,7 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
     tc_fence_after();
     const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kTileN;
     const int row = m0 + static_cast<int>(rank) * kTileRows + q * 32 + lane;
-    if ((!SK || (u.k0 == 0 && u.k1 == p.k_blocks)) && p.store_tma) {
+    if (STAGE && (!SK || (u.k0 == 0 && u.k1 == p.k_blocks)) && p.store_tma) {
       // fp32 (+ bias) -> fp16, staged per 64-column panel into a 128B-swizzled box
       // and written by one bulk tensor store: every global write is a full
       // 128-byte row segment instead of 32 scattered 16-byte pieces per warp store.
@@ -357,7 +365,7 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
     ++uidx;
   }
   // Stores must finish reading the staging boxes before the CTA exits.
-  if (lane == 0) bulk_wait_all();
+  if (STAGE && lane == 0) bulk_wait_all();
   __syncwarp();
 }
 
@@ -375,7 +383,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
   uint8_t* staging = smem + STAGES * C::kStageBytes;
   uint8_t* bar_area = staging + C::kStagingBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
-  uint64_t* decoded = full + STAGES;
+  uint64_t* raw_full = full + STAGES;  // used by the forward configuration only
+  uint64_t* decoded = raw_full + STAGES;
   uint64_t* empty = decoded + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -398,6 +407,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&raw_full[s], 1);
       mbar_init(&decoded[s], 2 * 128);
       mbar_init(&empty[s], 1);
     }
@@ -428,7 +438,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      tma_prefetch_desc(&tmA);  // tmB is unused: the decoders read packed codes directly
+      tma_prefetch_desc(&tmA);
+      if (C::kRawTma) tma_prefetch_desc(&tmB);
       if (has_lora) {
         tma_prefetch_desc(&tmLA);
         tma_prefetch_desc(&tmLB);
@@ -454,10 +465,15 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
           if (step < u.k1) {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kABytes);
             tma_load_2d_pair(a_s, &tmA, leader_full + 8u * s, step * kBK, arow);
+            if constexpr (C::kRawTma) {
+              mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
+              tma_load_2d(b_s + C::kBBytes, &tmB, &raw_full[s], step * (kBK / 2), brow);
+            }
           } else {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * (kTileRows + kHalfN) * p.lora_r * 2);
             tma_load_2d_pair(a_s, &tmLA, leader_full + 8u * s, 0, arow);
             tma_load_2d_pair(b_s, &tmLB, leader_full + 8u * s, 0, brow);
+            if constexpr (C::kRawTma) mbar_arrive(&raw_full[s]);  // nothing to decode
           }
         }
       }
@@ -469,10 +485,11 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
       for (uint32_t j = it; clean && j < it + STAGES; ++j) {
         clean = mbar_wait(&empty[j % STAGES], ((j / STAGES) & 1) ^ 1, kErrWaitDrain, abort_flag);
       }
-      if (!clean && leader) {
+      if (!clean) {
         const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0;
         for (uint32_t j = first; j < it; ++j) {
-          mbar_wait(&full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
+          if (C::kRawTma) mbar_wait(&raw_full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
+          if (leader) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
         }
       }
     }
@@ -539,8 +556,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
       warp_wait(drain, 0, kErrWaitDrain, &no_abort, lane);
     }
   } else if (warp >= 4 && warp < 8) {
-    if (lane == 0 && p.store_tma) tma_prefetch_desc(&tmY);
-    pair_epilogue<EMODE, SK>(p, &tmY, staging, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
+    if (lane == 0 && C::kStoreStage && p.store_tma) tma_prefetch_desc(&tmY);
+    pair_epilogue<EMODE, SK, C::kStoreStage>(p, &tmY, staging, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
                          num_tiles, rows_valid, pair_id, pairs, rank);
   } else if (warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders (both CTAs)
@@ -588,9 +605,11 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
       uint32_t q_next = 0u;
       float a2_next = 0.0f;
       if (nb >= 0) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, first));
-        w0_next = ld_stream16(src);
-        w1_next = ld_stream16(src + 1);
+        if constexpr (!C::kRawTma) {
+          const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, first));
+          w0_next = ld_stream16(src);
+          w1_next = ld_stream16(src + 1);
+        }
         q_next = __ldg(p.qabs + nb);
         a2_next = __ldg(p.absmax2 + (nb >> 8));
       }
@@ -606,17 +625,31 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
         const bool valid = main_step && block_of(n0, step) >= 0;
         nb = step + 2 < u.k1 ? block_of(n0, step + 2) : -1;
         if (nb >= 0) {
-          const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, step + 2));
-          w0_next = ld_stream16(src);
-          w1_next = ld_stream16(src + 1);
+          if constexpr (!C::kRawTma) {
+            const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, step + 2));
+            w0_next = ld_stream16(src);
+            w1_next = ld_stream16(src + 1);
+          }
           q_next = __ldg(p.qabs + nb);
           a2_next = __ldg(p.absmax2 + (nb >> 8));
         }
-        if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) { ok = false; break; }
+        // Forward: raw_full[s] (the producer loaded the packed codes after empty[s]).
+        // dX: empty[s] (the UMMA that read this B slot has completed).
+        if (C::kRawTma ? !mbar_wait(&raw_full[s], ph, kErrWaitFull, abort_flag)
+                       : !mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
         if (main_step) {
           uint8_t* b_s = smem + s * C::kStageBytes + C::kABytes;
           const float scale = valid ? __fadd_rn(__fmul_rn(code2_s[q_cur], a2_cur), off) : 0.0f;
-          if constexpr (BMODE == kNF4Fwd) {
+          if constexpr (C::kRawTma) {
+            // Packed rows are 32 B, TMA-swizzled in 32 B spans: chunk ^= (row >> 2) & 1.
+            const uint8_t* raw_s = b_s + C::kBBytes;
+            const uint32_t x = static_cast<uint32_t>((gtid >> 2) & 1);
+            nf4_decode_row(raw_s + gtid * 32 + (x << 4), raw_s + gtid * 32 + ((x ^ 1u) << 4), b_s + gtid * 128,
+                           gtid, scale, valid);
+          } else if constexpr (BMODE == kNF4Fwd) {
             nf4_decode_words(w0, w1, b_s + gtid * 128, gtid, scale, valid);
           } else {
             const int r = gtid >> 1, j = gtid & 1;
