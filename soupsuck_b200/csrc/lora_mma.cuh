@@ -106,6 +106,49 @@ __global__ void reduce_finalize_kernel(const float* __restrict__ partial, int sp
   st_from_f32(out, odt, transpose ? c * r + j : j * Wd + c, acc);
 }
 
+// Finalize with the splits spread over a CTA: 256 threads = 16 split groups x 16
+// float4 columns, so a CTA covers 64 consecutive values of one partial row
+// [r * Wd] and group q sums splits q, q + 16, ...; the 16 group sums are then
+// added in group order.  The order is fixed, so results are deterministic, and
+// every split's 64-value row segment is read by 16 threads at once (the
+// one-thread-per-output kernel above serialises up to a few hundred loads).
+// Requires Wd % 4 == 0 (float4 rows).
+__global__ void __launch_bounds__(256) reduce_finalize2_kernel(const float* __restrict__ partial, int splits,
+                                                               int64_t Wd, int r, float scale, int transpose,
+                                                               void* __restrict__ out, int odt) {
+  __shared__ float4 part[16][17];
+  const int col4 = threadIdx.x & 15, grp = threadIdx.x >> 4;
+  const int64_t total4 = Wd * r / 4;
+  const int64_t e4 = static_cast<int64_t>(blockIdx.x) * 16 + col4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (e4 < total4) {
+    const float4* src = reinterpret_cast<const float4*>(partial) + e4;
+    const int64_t split4 = total4;
+#pragma unroll 4
+    for (int s = grp; s < splits; s += 16) {
+      const float4 v = __ldcg(src + static_cast<int64_t>(s) * split4);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+  }
+  part[grp][col4] = acc;
+  __syncthreads();
+  if (grp == 0 && e4 < total4) {
+    float4 t = part[0][col4];
+#pragma unroll
+    for (int q = 1; q < 16; ++q) {
+      const float4 v = part[q][col4];
+      t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+    }
+    const float vals[4] = {t.x * scale, t.y * scale, t.z * scale, t.w * scale};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t e = e4 * 4 + i;
+      const int64_t j = e / Wd, c = e % Wd;
+      st_from_f32(out, odt, transpose ? c * r + j : j * Wd + c, vals[i]);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ streamed variants
 // The two kernels above keep few bytes in flight (4-byte loads in the reduction,
 // one 16-row tile of 4 warps in the projection).  The streamed variants below
@@ -467,6 +510,12 @@ int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m
     if (int rc = sb::check_launch("lora_reduce_partial_kernel")) return rc;
   }
   const int64_t total = w * r;
+  if (w % 4 == 0) {
+    sb::lora::reduce_finalize2_kernel<<<static_cast<unsigned>((total / 4 + 15) / 16), 256, 0, st>>>(
+        partial, splits, w, r, scale, transpose, out, out_dtype);
+    sb::count_launch();
+    return sb::check_launch("lora_reduce_finalize2_kernel");
+  }
   sb::lora::reduce_finalize_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
       partial, splits, w, r, scale, transpose, out, out_dtype);
   sb::count_launch();

@@ -86,6 +86,152 @@ __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_fwd_kernel(
   if (threadIdx.x == 0) rstd_out[row] = r;
 }
 
+// ------------------------------------------- fp16 fast path of add + RMSNorm
+// The training configuration (fp16 residual, delta, gamma, s and y; contiguous
+// rows; H % 8 == 0) reads and writes every row as 16-byte vectors and keeps the
+// row in registers: thread t of the row's CTA owns the 8-element pieces t,
+// t + T, ... (V of them).  The cast order is the reference's, as above; only the
+// order of the fp32 sum of squares differs (per-thread pieces, then the block).
+__device__ __forceinline__ void h8_to_f32(const uint4& v, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 f32_to_h8(const float (&f)[8]) {
+  uint4 v;
+  __half2* h = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+__device__ __forceinline__ float f16_round(float v) { return __half2float(__float2half_rn(v)); }
+
+template <int T>
+__device__ __forceinline__ float block_sum_t(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int w = 0; w < T / 32; ++w) total += scratch[w];
+  return total;
+}
+
+template <int T, int V>
+__global__ void __launch_bounds__(T) add_rmsnorm_fwd_h8_kernel(const uint4* __restrict__ R,
+                                                               const uint4* __restrict__ D,
+                                                               const uint4* __restrict__ W, uint4* __restrict__ S,
+                                                               uint4* __restrict__ Y, float* __restrict__ rstd_out,
+                                                               int64_t h, float eps) {
+  __shared__ float scratch[T / 32];
+  const int64_t h8 = h / 8;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * h8;
+  float s[V][8];
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int64_t c = threadIdx.x + static_cast<int64_t>(i) * T;
+    if (c < h8) {
+      float r8[8], d8[8];
+      h8_to_f32(__ldcs(R + base + c), r8);
+      h8_to_f32(__ldcs(D + base + c), d8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s[i][e] = f16_round(__fadd_rn(r8[e], d8[e]));
+        acc = __fadd_rn(acc, __fmul_rn(s[i][e], s[i][e]));
+      }
+      S[base + c] = f32_to_h8(s[i]);
+    }
+  }
+  const float total = block_sum_t<T>(acc, scratch);
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(h)), eps));
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int64_t c = threadIdx.x + static_cast<int64_t>(i) * T;
+    if (c < h8) {
+      float w8[8], y8[8];
+      h8_to_f32(__ldg(W + c), w8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y8[e] = __fmul_rn(f16_round(__fmul_rn(s[i][e], r)), w8[e]);
+      Y[base + c] = f32_to_h8(y8);
+    }
+  }
+  if (threadIdx.x == 0) rstd_out[blockIdx.x] = r;
+}
+
+template <int T, int V>
+__global__ void __launch_bounds__(T) add_rmsnorm_bwd_h8_kernel(const uint4* __restrict__ Sv,
+                                                               const uint4* __restrict__ W,
+                                                               const float* __restrict__ rstd,
+                                                               const uint4* __restrict__ Gs, int64_t gs_row8,
+                                                               const uint4* __restrict__ Gy, int64_t gy_row8,
+                                                               uint4* __restrict__ Dr, uint4* __restrict__ Dd,
+                                                               int64_t h) {
+  __shared__ float scratch[T / 32];
+  const int64_t h8 = h / 8;
+  const int64_t row = blockIdx.x;
+  const int64_t base = row * h8;
+  float u[V][8], a[V][8];
+  float proj = 0.0f, r = 0.0f;
+  if (Gy != nullptr) {
+    r = rstd[row];
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int64_t c = threadIdx.x + static_cast<int64_t>(i) * T;
+      if (c < h8) {
+        float s8[8], g8[8], w8[8];
+        h8_to_f32(__ldcs(Sv + base + c), s8);
+        h8_to_f32(__ldcs(Gy + row * gy_row8 + c), g8);
+        h8_to_f32(__ldg(W + c), w8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          a[i][e] = __fmul_rn(s8[e], r);
+          u[i][e] = f16_round(__fmul_rn(g8[e], w8[e]));
+          acc = __fadd_rn(acc, __fmul_rn(u[i][e], a[i][e]));
+        }
+      }
+    }
+    proj = __fdiv_rn(block_sum_t<T>(acc, scratch), static_cast<float>(h));
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int64_t c = threadIdx.x + static_cast<int64_t>(i) * T;
+    if (c < h8) {
+      float gs8[8], ds[8];
+      if (Gs != nullptr) h8_to_f32(__ldcs(Gs + row * gs_row8 + c), gs8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float d = 0.0f;
+        if (Gy != nullptr) d = f16_round(__fmul_rn(r, __fsub_rn(u[i][e], __fmul_rn(a[i][e], proj))));
+        if (Gs != nullptr) d = __fadd_rn(d, gs8[e]);
+        ds[e] = f16_round(d);
+      }
+      const uint4 o = f32_to_h8(ds);
+      if (Dr != nullptr) Dr[base + c] = o;
+      if (Dd != nullptr) Dd[base + c] = o;
+    }
+  }
+}
+
+// 16-byte pieces per thread of the fast path (256 threads per row), 0 if H does
+// not qualify (H % 8 != 0 or H > 8192).
+constexpr int kH8Threads = 256;
+inline int h8_pieces(int64_t h) {
+  if (h % 8 != 0) return 0;
+  const int64_t h8 = h / 8;
+  for (int v : {1, 2, 4}) {
+    if (h8 <= static_cast<int64_t>(v) * kH8Threads) return v;
+  }
+  return 0;
+}
+
 // add_rmsnorm_backward_kernel (solution/kernels/add_rmsnorm.py:54-81).
 __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_bwd_kernel(
     const void* __restrict__ S, int sdt, const void* __restrict__ W, int wdt, int64_t w_stride,
@@ -255,6 +401,24 @@ int sb_add_rmsnorm_fwd(const void* residual, int r_dtype, const void* delta, int
   if (rows == 0) return SB_OK;
   SB_REQUIRE(residual && delta && weight && s && y && rstd, "NULL pointer argument");
   SB_REQUIRE(rows <= 0x7fffffff, "too many rows");
+  const int pieces = sb::h8_pieces(h);
+  if (pieces && r_dtype == SB_F16 && d_dtype == SB_F16 && w_dtype == SB_F16 && y_dtype == SB_F16 &&
+      w_stride == 1 && sb::aligned(residual, 16) && sb::aligned(delta, 16) && sb::aligned(weight, 16) &&
+      sb::aligned(s, 16) && sb::aligned(y, 16)) {
+    const uint4* R = static_cast<const uint4*>(residual);
+    const uint4* D = static_cast<const uint4*>(delta);
+    const uint4* W = static_cast<const uint4*>(weight);
+    uint4* S = static_cast<uint4*>(s);
+    uint4* Y = static_cast<uint4*>(y);
+    constexpr int T = sb::kH8Threads;
+    const unsigned grid = static_cast<unsigned>(rows);
+    cudaStream_t st = sb::as_stream(stream);
+    if (pieces == 1) sb::add_rmsnorm_fwd_h8_kernel<T, 1><<<grid, T, 0, st>>>(R, D, W, S, Y, rstd, h, eps);
+    else if (pieces == 2) sb::add_rmsnorm_fwd_h8_kernel<T, 2><<<grid, T, 0, st>>>(R, D, W, S, Y, rstd, h, eps);
+    else sb::add_rmsnorm_fwd_h8_kernel<T, 4><<<grid, T, 0, st>>>(R, D, W, S, Y, rstd, h, eps);
+    sb::count_launch();
+    return sb::check_launch("add_rmsnorm_fwd_h8_kernel");
+  }
   sb::add_rmsnorm_fwd_kernel<<<static_cast<unsigned>(rows), sb::kRowThreads, h * sizeof(float),
                                sb::as_stream(stream)>>>(residual, r_dtype, delta, d_dtype, weight,
                                                         w_dtype, w_stride, s, y, y_dtype, rstd,
@@ -278,6 +442,29 @@ int sb_add_rmsnorm_bwd(const void* s, int s_dtype, const void* weight, int w_dty
   if (rows == 0 || (!dr && !dd)) return SB_OK;
   SB_REQUIRE(s && weight && (rstd || !gy), "NULL pointer argument");
   SB_REQUIRE(rows <= 0x7fffffff, "too many rows");
+  const int pieces = sb::h8_pieces(h);
+  const bool gs_ok = !gs || (gs_dtype == SB_F16 && gs_col == 1 && gs_row % 8 == 0 && sb::aligned(gs, 16));
+  const bool gy_ok = !gy || (gy_dtype == SB_F16 && gy_col == 1 && gy_row % 8 == 0 && sb::aligned(gy, 16));
+  const bool out_ok = (!dr || (dr_dtype == SB_F16 && sb::aligned(dr, 16))) &&
+                      (!dd || (dd_dtype == SB_F16 && sb::aligned(dd, 16)));
+  if (pieces && s_dtype == SB_F16 && w_dtype == SB_F16 && w_stride == 1 && sb::aligned(s, 16) &&
+      sb::aligned(weight, 16) && gs_ok && gy_ok && out_ok) {
+    const uint4* S = static_cast<const uint4*>(s);
+    const uint4* W = static_cast<const uint4*>(weight);
+    const uint4* GS = static_cast<const uint4*>(gs);
+    const uint4* GY = static_cast<const uint4*>(gy);
+    uint4* DR = static_cast<uint4*>(dr);
+    uint4* DD = static_cast<uint4*>(dd);
+    constexpr int T = sb::kH8Threads;
+    const unsigned grid = static_cast<unsigned>(rows);
+    cudaStream_t st = sb::as_stream(stream);
+    const int64_t gs8 = gs_row / 8, gy8 = gy_row / 8;
+    if (pieces == 1) sb::add_rmsnorm_bwd_h8_kernel<T, 1><<<grid, T, 0, st>>>(S, W, rstd, GS, gs8, GY, gy8, DR, DD, h);
+    else if (pieces == 2) sb::add_rmsnorm_bwd_h8_kernel<T, 2><<<grid, T, 0, st>>>(S, W, rstd, GS, gs8, GY, gy8, DR, DD, h);
+    else sb::add_rmsnorm_bwd_h8_kernel<T, 4><<<grid, T, 0, st>>>(S, W, rstd, GS, gs8, GY, gy8, DR, DD, h);
+    sb::count_launch();
+    return sb::check_launch("add_rmsnorm_bwd_h8_kernel");
+  }
   sb::add_rmsnorm_bwd_kernel<<<static_cast<unsigned>(rows), sb::kRowThreads,
                                2 * h * sizeof(float), sb::as_stream(stream)>>>(
       s, s_dtype, weight, w_dtype, w_stride, rstd, gs, gs_dtype, gs_row, gs_col, gy, gy_dtype,
