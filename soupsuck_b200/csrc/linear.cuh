@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "gemm_host.cuh"
 #include "nf4_smallm.cuh"
+#include "nf4_lut.cuh"
 #include "nf4_dequant.cuh"
 
 namespace sb {
@@ -89,6 +90,14 @@ inline int nf4_linear_fallback(bool dx, const uint16_t* act, int64_t m, const sb
   return check_launch("fallback_gemm_kernel");
 }
 
+// Small-M kernel choice: SB_SMALLM=mma takes the decode-to-shared mma.sync kernel
+// (nf4_smallm.cuh); unset or "lut" the table-lookup kernel (nf4_lut.cuh) where it
+// applies.  Read per call.
+inline int smallm_kernel() {
+  const char* e = std::getenv("SB_SMALLM");
+  return (e && std::string(e) == "mma") ? 1 : 0;
+}
+
 // Activations of at most 16 rows take the streaming small-M kernel (weight-read bound).
 inline bool smallm_ok(int64_t m, int64_t n_out, int64_t k_in, bool dx) {
   return m >= 1 && m <= smallm::kRows && k_in % 64 == 0 && (!dx || n_out % 8 == 0) &&
@@ -111,6 +120,9 @@ inline int nf4_linear(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weig
                        (r == 0 || (aligned(lora_a, 16) && aligned(lora_b, 16)));
   if (smallm_ok(m, w->n_out, w->k_in, dx) && aligned(act, 16) && aligned(w->packed, 16) &&
       (r == 0 || (aligned(lora_a, 2) && aligned(lora_b, 2)))) {
+    if (!dx && lut::fwd_ok(m, w->n_out, w->k_in) && smallm_kernel() == 0) {
+      return lut::run_fwd(act, m, *w, bias, lora_a, lora_b, r, out, st);
+    }
     return smallm::run(dx, act, m, *w, bias, lora_a, lora_b, r, out, workspace, workspace_bytes, st);
   }
   if (tc_rank && ptrs_ok && gemm::nf4_tc_shape_ok(m, w->n_out, w->k_in, dx)) {

@@ -1,0 +1,444 @@
+// Small-M NF4 linear (M <= 16 activation rows) by table lookup: forward Y = X . deq(W)^T.
+//
+// At M <= 16 the product is bound by reading the packed weight (0.52 byte per
+// weight), so the limit is how few instructions turn a packed byte into MMA
+// operands.  Here one shared-memory load does it:
+//
+//   * a 256-entry table maps a packed byte (two codes, the earlier element in the
+//     high nibble) to the half2 (NF4[hi], NF4[lo]) of the two UNSCALED code
+//     values.  Every lane has its own copy of the table (entry e of lane l at
+//     byte e * 128 + 4 l), so a warp's 32 lookups hit 32 different banks;
+//   * the block scale s(n, b) = fp32(code2[absmax[n, b]] * absmax2) + offset of
+//     the bitsandbytes format multiplies, in fp32, the partial product of each
+//     64-element block after its four mma.sync.m16n8k16 steps (the scale is
+//     constant inside a block and an MMA never straddles two blocks).
+//
+// The weight is the MMA's A operand (16 weight rows per warp tile) and the
+// activations its B operand (8 or 16 tokens).  Inside a 64-element block,
+// lane t of a quad holds the packed bytes 8t .. 8t + 7 (elements 16t .. 16t + 15)
+// of its two rows; k-step j of the block uses bytes 8t + 2j and 8t + 2j + 1, and
+// the activation fragment is permuted the same way, so each lane reads one 8-byte
+// piece of each row per block straight from global memory (no staging, no
+// decoded tile) and its activations as two 16-byte shared-memory loads.
+//
+// Work split: a CTA of 8 warps covers RW row tiles (16 rows each) x KW k-runs
+// (RW * KW = 8); a cluster of S CTAs along grid.y splits the reduction, and the
+// partial sums are combined in fixed rank order through distributed shared
+// memory, then bias and the LoRA term are added and fp16 rows stored.  One launch,
+// no global scratch, deterministic.
+//
+// Numerics: the weights enter the MMA as fp16(NF4[i]) and the scale is applied in
+// fp32 per block, instead of the reference decoder's fp16(NF4[i] * scale) --
+// a different rounding of the same product, inside the GEMM gate (the standalone
+// decoder stays bit-exact).
+//
+// Reference: bitsandbytes' MatMul4Bit / gemv_4bit small-batch path behind
+// solution/nf4_patch.py:43-125; decode rule solution/kernels/nf4.py:41-59.
+#pragma once
+
+#include "common.cuh"
+#include "gemm_pair.cuh"
+#include "lora_mma.cuh"
+
+namespace sb {
+namespace lut {
+
+constexpr int kThreads = 256, kWarps = 8;
+constexpr int kGroup = 4;                 // 64-blocks per load group (one absmax word per row)
+constexpr int kMaxSplits = 8;             // cluster size along the reduction (portable)
+constexpr int64_t kMaxReduction = 9216;   // longest reduction on this path (its error grows as sqrt)
+
+// The table holds fp16(kAlpha * NF4[i]); the block scale is multiplied by 1/kAlpha
+// in fp32.  kAlpha minimises the RMS relative rounding error of the 15 nonzero
+// fp16 entries (9.2e-5 against 1.8e-4 at alpha = 1), found by scanning alpha over
+// [1, 2) in steps of 2^-16.
+constexpr float kAlpha = 1.3661651611328125f;
+constexpr float kInvAlpha = 1.0f / 1.3661651611328125f;
+
+// Per-lane byte -> half2 table (32 KB, static so its base folds into the loads).
+__device__ __forceinline__ void build_table(uint32_t* table) {
+  for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) {
+    const int e = i >> 3, part = i & 7;
+    const __half2 v = __floats2half2_rn(kAlpha * c_nf4_values[e >> 4], kAlpha * c_nf4_values[e & 15]);
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(&v);
+    *reinterpret_cast<uint4*>(table + e * 32 + part * 4) = make_uint4(u, u, u, u);
+  }
+}
+
+// Byte `I` (0..3) of `w` looked up in this lane's table copy; `tb` is the 32-bit
+// shared address of the table plus 4 * lane.
+template <int I>
+__device__ __forceinline__ uint32_t lookup(uint32_t tb, uint32_t w) {
+  uint32_t off;
+  if constexpr (I == 0) off = (w << 7) & 0x7F80u;
+  else if constexpr (I == 1) off = (w >> 1) & 0x7F80u;
+  else if constexpr (I == 2) off = (w >> 9) & 0x7F80u;
+  else off = (w >> 17) & 0x7F80u;
+  uint32_t v;
+  asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(tb + off));
+  return v;
+}
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
+// m16n8k16 with a zero accumulator input (no register moves to clear it).
+__device__ __forceinline__ void mma16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+struct FwdArgs {
+  const __half* x;        // [M, K] row-major
+  int M;
+  int64_t K, N;           // reduction length (k_in), output columns (n_out)
+  const uint8_t* packed;
+  const uint8_t* qabs;
+  const float* absmax2;
+  const float* code2;
+  const float* offset;
+  int rw, kw;             // warp layout: rw row tiles x kw k-runs
+  int kb_split;           // 64-blocks of the reduction per cluster rank
+  int splits;             // cluster size along grid.y
+  const __half* bias;     // [N] or null
+  const __half* la;       // [M, r] (LoRA: y += la . lb^T) or null
+  const __half* lb;       // [N, r]
+  int r;
+  __half* y;              // [M, N]
+};
+
+// Dynamic shared memory of the forward kernel: activation tile, code2 table,
+// per-warp fragments, CTA partial.
+template <int NT>
+struct FwdSmem {
+  static constexpr int kTok = 8 * NT;
+  __host__ __device__ static size_t pitch(int kb) { return static_cast<size_t>(kb) * 128 + 16; }
+  __host__ __device__ static size_t x_bytes(int kb) { return kTok * pitch(kb); }
+  static constexpr int kRedBytes = kWarps * 16 * 16 * 4;    // per-warp C fragments (aliases the tile)
+  static constexpr int kPartBytes = kWarps * 16 * 16 * 4;   // CTA partial [rows <= 128][16]
+  __host__ __device__ static size_t tile_bytes(int kb) { return x_bytes(kb) > kRedBytes ? x_bytes(kb) : kRedBytes; }
+  __host__ __device__ static size_t bytes(int kb) { return tile_bytes(kb) + 1024 + kPartBytes; }
+};
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
+  __shared__ __align__(128) uint32_t table[256 * 32];
+  extern __shared__ __align__(128) uint8_t dsm[];
+  using S = FwdSmem<NT>;
+  // Register ring of load groups: three slots (two groups in flight) for 8 token
+  // columns, two for 16 (their fragments need the registers).
+  constexpr int kSlots = NT == 1 ? 3 : 2;
+  constexpr int kAhead = kSlots - 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t lane4 = static_cast<uint32_t>(lane) << 2;
+  const uint32_t rank = gemm::pair::cluster_rank();
+  const int64_t kblocks = a.K / 64;
+  const int64_t kb0 = static_cast<int64_t>(rank) * a.kb_split;
+  int64_t kb1 = kb0 + a.kb_split;
+  if (kb1 > kblocks) kb1 = kblocks;
+  const int kb_cta = kb1 > kb0 ? static_cast<int>(kb1 - kb0) : 0;
+  const size_t pitch = S::pitch(a.kb_split);
+  uint8_t* xs = dsm;
+  float* red = reinterpret_cast<float*>(dsm);  // reused once every warp is past the tile
+  float* code2_s = reinterpret_cast<float*>(dsm + S::tile_bytes(a.kb_split));
+  float* part = code2_s + 256;
+
+  // Activation tile [8 NT tokens][kb_cta * 64] (zero rows past M) by cp.async.
+  {
+    const int chunks = kb_cta * 8;  // 16-byte pieces per token row
+    for (int i = tid; i < S::kTok * chunks; i += kThreads) {
+      const int tok = i / chunks, c = i % chunks;
+      const bool ok = tok < a.M;
+      const __half* src = ok ? a.x + tok * a.K + kb0 * 64 + c * 8 : a.x;
+      lora::cp_async16(smem_addr(xs + tok * pitch + c * 16), src, ok);
+    }
+    lora::cp_async_commit();
+  }
+  for (int i = tid; i < 256; i += kThreads) code2_s[i] = __ldg(a.code2 + i);
+  build_table(table);
+  const float off = __ldg(a.offset);
+
+  // This warp's row tile and k-run.
+  const int rw = warp % a.rw, kw = warp / a.rw;
+  const int64_t n_g = (static_cast<int64_t>(blockIdx.x) * a.rw + rw) * 16 + g;
+  const int64_t n_g8 = n_g + 8;
+  const bool ok_g = n_g < a.N, ok_g8 = n_g8 < a.N;
+  const int run = ((kb_cta + a.kw - 1) / a.kw + kGroup - 1) / kGroup * kGroup;
+  const int rb0 = kw * run;                               // first block (CTA-relative)
+  int rb1 = rb0 + run;
+  if (rb1 > kb_cta) rb1 = kb_cta;
+  const int nb = rb1 > rb0 ? rb1 - rb0 : 0;
+  const int64_t row_bytes = a.K / 2;
+  // Byte and block offsets of the weight fit 32 bits (checked by the host).
+  const uint8_t* p_g = a.packed + static_cast<uint32_t>((ok_g ? n_g : 0) * row_bytes + (kb0 + rb0) * 32 + 8 * t);
+  const uint8_t* p_g8 = a.packed + static_cast<uint32_t>((ok_g8 ? n_g8 : 0) * row_bytes + (kb0 + rb0) * 32 + 8 * t);
+  const uint32_t q_g = static_cast<uint32_t>((ok_g ? n_g : 0) * kblocks + kb0 + rb0);
+  const uint32_t q_g8 = static_cast<uint32_t>((ok_g8 ? n_g8 : 0) * kblocks + kb0 + rb0);
+  const int ng = nb / kGroup;  // runs are whole groups of four blocks
+
+  // Register ring of kSlots groups: per group the two rows' 8-byte pieces of four
+  // blocks, the four absmax bytes of each row (one 32-bit word: groups start on a
+  // multiple of four blocks) and the row's absmax2 (the same for the four blocks).
+  uint2 pk[kSlots][kGroup][2];
+  uint32_t qw[kSlots][2];
+  float a2[kSlots][2];
+  auto load = [&](int gi, int slot) {
+    if (gi < ng) {
+      const uint32_t boff = static_cast<uint32_t>(gi) * (kGroup * 32);
+#pragma unroll
+      for (int b = 0; b < kGroup; ++b) {
+        pk[slot][b][0] = __ldcs(reinterpret_cast<const uint2*>(p_g + boff + b * 32));
+        pk[slot][b][1] = __ldcs(reinterpret_cast<const uint2*>(p_g8 + boff + b * 32));
+      }
+      const uint32_t qo = static_cast<uint32_t>(gi) * kGroup;
+      qw[slot][0] = __ldg(reinterpret_cast<const uint32_t*>(a.qabs + q_g + qo));
+      qw[slot][1] = __ldg(reinterpret_cast<const uint32_t*>(a.qabs + q_g8 + qo));
+      a2[slot][0] = __ldg(a.absmax2 + ((q_g + qo) >> 8));
+      a2[slot][1] = __ldg(a.absmax2 + ((q_g8 + qo) >> 8));
+    }
+  };
+#pragma unroll
+  for (int q = 0; q < kAhead; ++q) load(q, q);
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+
+  lora::cp_async_wait<0>();
+  __syncthreads();  // table, code2 and activation tile ready
+
+  // Activation rows of this lane's B fragments (token g + 8 nt).
+  uint32_t xrow[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    xrow[nt] = smem_addr(xs) + static_cast<uint32_t>((g + 8 * nt) * pitch) + static_cast<uint32_t>(rb0) * 128 + 32 * t;
+  }
+  const float soff = off;
+  const uint32_t tb = smem_addr(table) + lane4;
+  const uint32_t c2s = smem_addr(code2_s);
+
+  for (int G = 0; G < ng; G += kSlots) {
+#pragma unroll
+    for (int sl = 0; sl < kSlots; ++sl) {
+      const int gi = G + sl;
+      if (gi < ng) {
+        load(gi + kAhead, (sl + kAhead) % kSlots);
+#pragma unroll
+        for (int b = 0; b < kGroup; ++b) {
+          const uint32_t blk = static_cast<uint32_t>(gi * kGroup + b);
+          const float s_g = ok_g ? __fmul_rn(__fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][0] >> (8 * b)) & 0xFFu) * 4), a2[sl][0]), soff), kInvAlpha) : 0.0f;
+          const float s_g8 = ok_g8 ? __fmul_rn(__fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][1] >> (8 * b)) & 0xFFu) * 4), a2[sl][1]), soff), kInvAlpha) : 0.0f;
+          // Activation B fragments (rows past M are zero in the tile).
+          uint32_t xf[NT][8];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint32_t addr = xrow[nt] + blk * 128;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(xf[nt][0]), "=r"(xf[nt][1]), "=r"(xf[nt][2]), "=r"(xf[nt][3]) : "r"(addr));
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(xf[nt][4]), "=r"(xf[nt][5]), "=r"(xf[nt][6]), "=r"(xf[nt][7]) : "r"(addr + 16));
+          }
+          float ct[NT][4];
+          const uint32_t wg[2] = {pk[sl][b][0].x, pk[sl][b][0].y}, wg8[2] = {pk[sl][b][1].x, pk[sl][b][1].y};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t af[4];
+            if ((j & 1) == 0) {
+              af[0] = lookup<0>(tb, wg[j >> 1]);
+              af[1] = lookup<0>(tb, wg8[j >> 1]);
+              af[2] = lookup<1>(tb, wg[j >> 1]);
+              af[3] = lookup<1>(tb, wg8[j >> 1]);
+            } else {
+              af[0] = lookup<2>(tb, wg[j >> 1]);
+              af[1] = lookup<2>(tb, wg8[j >> 1]);
+              af[2] = lookup<3>(tb, wg[j >> 1]);
+              af[3] = lookup<3>(tb, wg8[j >> 1]);
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (j == 0) mma16816_z(ct[nt], af, xf[nt][0], xf[nt][1]);
+              else lora::mma16816(ct[nt], af, xf[nt][2 * j], xf[nt][2 * j + 1]);
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] = fmaf(s_g, ct[nt][0], acc[nt][0]);
+            acc[nt][1] = fmaf(s_g, ct[nt][1], acc[nt][1]);
+            acc[nt][2] = fmaf(s_g8, ct[nt][2], acc[nt][2]);
+            acc[nt][3] = fmaf(s_g8, ct[nt][3], acc[nt][3]);
+          }
+        }
+      }
+    }
+  }
+
+  // Intra-CTA: warps of the same row tile (different k-runs) add in k-run order.
+  __syncthreads();  // the activation tile is dead: its space takes the fragments
+  {
+    float* mine = red + warp * 256;  // [16 rows][16 tokens]
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int tok = 8 * nt + 2 * t;
+      mine[g * 16 + tok] = acc[nt][0];
+      mine[g * 16 + tok + 1] = acc[nt][1];
+      mine[(g + 8) * 16 + tok] = acc[nt][2];
+      mine[(g + 8) * 16 + tok + 1] = acc[nt][3];
+    }
+  }
+  __syncthreads();
+  const int rows_cta = a.rw * 16;
+  for (int e = tid; e < rows_cta * 16; e += kThreads) {
+    const int row = e >> 4, tok = e & 15;
+    const int tile = row >> 4;
+    float v = 0.0f;
+    for (int q = 0; q < a.kw; ++q) v += red[(q * a.rw + tile) * 256 + (row & 15) * 16 + tok];
+    part[e] = v;
+  }
+  // Cluster: rank q finishes its contiguous share of the CTA's rows, summing the
+  // partials of all ranks in rank order through distributed shared memory.
+  gemm::pair::cluster_sync_all();
+  const uint32_t part_s = smem_addr(part);
+  const int share = (rows_cta + a.splits - 1) / a.splits;
+  const int row0 = static_cast<int>(rank) * share;
+  const int nrows = row0 < rows_cta ? (rows_cta - row0 < share ? rows_cta - row0 : share) : 0;
+  const int64_t n_base = static_cast<int64_t>(blockIdx.x) * rows_cta;
+  for (int e = tid; e < nrows * a.M; e += kThreads) {
+    const int tok = e / nrows, row = row0 + e % nrows;
+    const int64_t n = n_base + row;
+    if (n >= a.N) continue;
+    float v = 0.0f;
+    for (int q = 0; q < a.splits; ++q) {
+      const uint32_t addr = gemm::pair::map_to_rank(part_s + static_cast<uint32_t>((row * 16 + tok) * 4), q);
+      float pv;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(addr) : "memory");
+      v += pv;
+    }
+    if (a.r > 0) {
+      float l = 0.0f;
+      for (int j = 0; j < a.r; ++j) l = fmaf(__half2float(a.la[tok * a.r + j]), __half2float(a.lb[n * a.r + j]), l);
+      v += l;
+    }
+    if (a.bias) v = __fadd_rn(v, __half2float(a.bias[n]));
+    a.y[static_cast<int64_t>(tok) * a.N + n] = __float2half_rn(v);
+  }
+  gemm::pair::cluster_sync_all();  // no CTA leaves while another reads its partial
+}
+
+// ------------------------------------------------------------------ host side
+struct FwdPlan {
+  int nt, rw, kw, kb_split, splits;
+  int64_t groups;
+  size_t smem;
+};
+
+inline int fwd_slots(int nt) {
+  // Two CTAs per SM (the kernel is launched with 2 blocks per SM as bound).
+  (void)nt;
+  return 2 * device_sm_count();
+}
+
+inline FwdPlan fwd_plan(int64_t m, int64_t n, int64_t k) {
+  FwdPlan best{};
+  best.nt = m <= 8 ? 1 : 2;
+  const int kb_max = best.nt == 1 ? 64 : 32;
+  const int64_t kblocks = k / 64, row_tiles = (n + 15) / 16;
+  const int slots = fwd_slots(best.nt);
+  double best_cost = 1e30;
+  for (int s = 1; s <= kMaxSplits; ++s) {
+    const int64_t kb = ((kblocks + s - 1) / s + kGroup - 1) / kGroup * kGroup;
+    if (kb > kb_max) continue;
+    const int64_t splits = (kblocks + kb - 1) / kb;
+    for (int rw : {8, 4, 2, 1}) {
+      const int kw = kWarps / rw;
+      const int64_t groups = (row_tiles + rw - 1) / rw;
+      const int64_t ctas = groups * splits;
+      const int64_t run = ((kb + kw - 1) / kw + kGroup - 1) / kGroup * kGroup;
+      const int64_t waves = (ctas + slots - 1) / slots;
+      // Per CTA: table build + activation tile + reduction, about two blocks' time.
+      const double cost = static_cast<double>(waves) * static_cast<double>(run + 2);
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best.rw = rw;
+        best.kw = kw;
+        best.kb_split = static_cast<int>(kb);
+        best.splits = static_cast<int>(splits);
+        best.groups = groups;
+      }
+    }
+  }
+  best.smem = best.nt == 1 ? FwdSmem<1>::bytes(best.kb_split) : FwdSmem<2>::bytes(best.kb_split);
+  return best;
+}
+
+inline bool fwd_ok(int64_t m, int64_t n, int64_t k) {
+  return m >= 1 && m <= 16 && k % (64 * kGroup) == 0 && k <= kMaxReduction &&
+         n * (k / 2) < (int64_t(1) << 32);
+}
+
+template <int NT>
+inline int launch_fwd(const FwdPlan& pl, const FwdArgs& a, cudaStream_t st) {
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(lut_fwd_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(FwdSmem<NT>::bytes(NT == 1 ? 64 : 32)));
+      if (e != cudaSuccess) return fail(SB_ECUDA, std::string("lut fwd smem attribute: ") + cudaGetErrorString(e));
+      configured[dev] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.groups), static_cast<unsigned>(pl.splits), 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(pl.splits);
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lut_fwd_kernel<NT>, a);
+  if (e != cudaSuccess) return fail(SB_ECUDA, std::string("lut_fwd_kernel launch: ") + cudaGetErrorString(e));
+  count_launch();
+  return check_launch("lut_fwd_kernel");
+}
+
+inline int run_fwd(const uint16_t* act, int64_t m, const sb_nf4_weight& w, const uint16_t* bias,
+                   const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* out, cudaStream_t st) {
+  const FwdPlan pl = fwd_plan(m, w.n_out, w.k_in);
+  FwdArgs a{};
+  a.x = reinterpret_cast<const __half*>(act);
+  a.M = static_cast<int>(m);
+  a.K = w.k_in;
+  a.N = w.n_out;
+  a.packed = w.packed;
+  a.qabs = w.qabs;
+  a.absmax2 = w.absmax2;
+  a.code2 = w.code2;
+  a.offset = w.offset;
+  a.rw = pl.rw;
+  a.kw = pl.kw;
+  a.kb_split = pl.kb_split;
+  a.splits = pl.splits;
+  a.bias = reinterpret_cast<const __half*>(bias);
+  a.la = reinterpret_cast<const __half*>(lora_a);
+  a.lb = reinterpret_cast<const __half*>(lora_b);
+  a.r = r;
+  a.y = reinterpret_cast<__half*>(out);
+  return pl.nt == 1 ? launch_fwd<1>(pl, a, st) : launch_fwd<2>(pl, a, st);
+}
+
+}  // namespace lut
+}  // namespace sb
