@@ -165,8 +165,14 @@ def input_shapes(t):
             "g_up": (t, INTER), "g_out": (t, HIDDEN)}
 
 
-def layer_step(torch, layer, inp):
-    """Forward + backward of the hot path of one decoder layer (public API calls)."""
+def layer_step(torch, layer, inp, streams=None):
+    """Forward + backward of the hot path of one decoder layer (public API calls).
+
+    With ``streams`` (two side streams) the projections that do not depend on each
+    other run concurrently: o_proj and down_proj (their inputs are layer inputs)
+    on one side stream, k/v beside q and up beside gate on the other.  Autograd
+    runs every backward node on the stream of its forward, so the backward
+    overlaps the same way; all streams are joined before returning."""
     from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear
     s = ALPHA / RANK_R
 
@@ -174,15 +180,40 @@ def layer_step(torch, layer, inp):
         packed, st, a, b = layer[name]
         return nf4_lora_linear(x, packed, st, a, b, s)
 
+    grads = [inp["g_q"], inp["g_k"], inp["g_v"], inp["g_gate"], inp["g_up"], inp["g_out"]]
+    if streams is None:
+        s1, y1 = add_rms_norm(inp["residual"], inp["mlp_prev"], layer["gamma_in"], EPS)
+        q, k, v = proj("q", y1), proj("k", y1), proj("v", y1)
+        o = proj("o", inp["attn"])
+        s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
+        gate, up = proj("gate", y2), proj("up", y2)
+        down = proj("down", inp["act"])
+        out = s2 + down
+        torch.autograd.backward([q, k, v, gate, up, out], grads)
+        return inp["residual"].grad
+    main = torch.cuda.current_stream()
+    sa, sb = streams
+    sa.wait_stream(main)
+    sb.wait_stream(main)
+    with torch.cuda.stream(sb):
+        o = proj("o", inp["attn"])
+        down = proj("down", inp["act"])
     s1, y1 = add_rms_norm(inp["residual"], inp["mlp_prev"], layer["gamma_in"], EPS)
-    q, k, v = proj("q", y1), proj("k", y1), proj("v", y1)
-    o = proj("o", inp["attn"])
+    sa.wait_stream(main)
+    with torch.cuda.stream(sa):
+        k, v = proj("k", y1), proj("v", y1)
+    q = proj("q", y1)
+    main.wait_stream(sb)
     s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
-    gate, up = proj("gate", y2), proj("up", y2)
-    down = proj("down", inp["act"])
+    sa.wait_stream(main)
+    with torch.cuda.stream(sa):
+        up = proj("up", y2)
+    gate = proj("gate", y2)
     out = s2 + down
-    torch.autograd.backward([q, k, v, gate, up, out],
-                            [inp["g_q"], inp["g_k"], inp["g_v"], inp["g_gate"], inp["g_up"], inp["g_out"]])
+    main.wait_stream(sa)
+    torch.autograd.backward([q, k, v, gate, up, out], grads)
+    main.wait_stream(sa)
+    main.wait_stream(sb)
     return inp["residual"].grad
 
 
@@ -495,6 +526,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=T_TOKENS)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-streams", action="store_true",
+                    help="run the layer's projections one after another on one stream")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ce", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -561,9 +594,11 @@ def main():
             p.grad.copy_(flat[off:off + n].view_as(p))
             off += n
 
+    streams = None if args.no_streams else (torch.cuda.Stream(device), torch.cuda.Stream(device))
+
     def device_step():
         zero_grads()
-        layer_step(torch, layer, dev_in)
+        layer_step(torch, layer, dev_in, streams)
         allreduce_grads()
 
     # Warm-up (also configures kernels before any capture).
@@ -585,7 +620,7 @@ def main():
         zero_grads()
         before = _lib.launch_count()
         with torch.cuda.graph(graph):
-            layer_step(torch, layer, dev_in)
+            layer_step(torch, layer, dev_in, streams)
         launches_per_step = _lib.launch_count() - before
         for _ in range(2):
             graph.replay()
@@ -694,7 +729,8 @@ def main():
                    "tokens_per_gpu": t, "global_tokens": t * world,
                    "parallelism": f"dp{world}" + (" + LoRA-grad NCCL all-reduce" if world > 1 else ""),
                    "l2": "flushed (256 MiB write) before every timed step, outside the events",
-                   "cuda_graph": graph is not None},
+                   "cuda_graph": graph is not None,
+                   "streams": "o/down, k/v and up on two side streams" if streams else "one stream"},
         "pct_peak": 100.0 * value / peak_burst,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": 1000 * e2e_sec},
