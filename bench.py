@@ -739,7 +739,7 @@ def main():
                      "frac": achieved / peak_burst, "traffic": measured_pass_traffic(t),
                      "traffic_unit": "DRAM bytes per pass of the 14 launches (ncu, profiles/nf4_gemm_pass_t3300_traffic.md)",
                      "algorithmic_bytes": pass_bytes(t),
-                     "kernel": "gemm_kernel<NF4> fwd+dX, LoRA fused",
+                     "kernel": "pair_kernel<NF4> (cta_group::2) fwd+dX, LoRA fused",
                      "peak_source": f"{peak_kind} bf16 dense burst (MEASURED_PEAKS.json)",
                      "launches": glaunch, "ms_per_pass": 1000 * gsec},
         "clocks": clocks.summary(),
