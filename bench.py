@@ -501,8 +501,8 @@ def run_sweep(args, torch):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             sec = float(tt.item())
         results.append({"M": m, "ms_per_pass": 1000 * sec, "tflops": flops / sec / 1e12,
-                        "pct_peak": 100 * flops / sec / 1e12 / peak_burst,
-                        "hbm_gbs": nbytes / sec / 1e9, "pct_hbm": 100 * nbytes / sec / 1e9 / hbm,
+                        "pct_peak": 100 * flops / sec / 1e12 / (peak_burst * world),
+                        "hbm_gbs": nbytes / sec / 1e9, "pct_hbm": 100 * nbytes / sec / 1e9 / (hbm * world),
                         "projection_calls": len(calls), "cuda_graph": world == 1 and not args.no_graph})
     err = _lib.take_device_error(device)
     if rank == 0:
