@@ -90,12 +90,16 @@ inline int nf4_linear_fallback(bool dx, const uint16_t* act, int64_t m, const sb
   return check_launch("fallback_gemm_kernel");
 }
 
-// Small-M kernel choice: SB_SMALLM=mma takes the decode-to-shared mma.sync kernel
-// (nf4_smallm.cuh); unset or "lut" the table-lookup kernel (nf4_lut.cuh) where it
-// applies.  Read per call.
+// Small-M forward kernel choice, read per call: SB_SMALLM=mma takes the
+// decode-to-shared mma.sync kernel (nf4_smallm.cuh), "lut" the unscaled-table
+// lookup mode of nf4_lut.cuh (reductions <= 9216), "exact" its exact-decode
+// mode; unset takes the exact mode.
+enum SmallmKernel { kSmallmExact = 0, kSmallmLut = 1, kSmallmMma = 2 };
 inline int smallm_kernel() {
   const char* e = std::getenv("SB_SMALLM");
-  return (e && std::string(e) == "mma") ? 1 : 0;
+  if (!e || !*e) return kSmallmExact;
+  const std::string v(e);
+  return v == "mma" ? kSmallmMma : (v == "lut" ? kSmallmLut : kSmallmExact);
 }
 
 // Activations of at most 16 rows take the streaming small-M kernel (weight-read bound).
@@ -120,8 +124,9 @@ inline int nf4_linear(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weig
                        (r == 0 || (aligned(lora_a, 16) && aligned(lora_b, 16)));
   if (smallm_ok(m, w->n_out, w->k_in, dx) && aligned(act, 16) && aligned(w->packed, 16) &&
       (r == 0 || (aligned(lora_a, 2) && aligned(lora_b, 2)))) {
-    if (!dx && lut::fwd_ok(m, w->n_out, w->k_in) && smallm_kernel() == 0) {
-      return lut::run_fwd(act, m, *w, bias, lora_a, lora_b, r, out, st);
+    const int kind = smallm_kernel();
+    if (!dx && kind != kSmallmMma && lut::fwd_ok(m, w->n_out, w->k_in, kind == kSmallmExact)) {
+      return lut::run_fwd(act, m, *w, bias, lora_a, lora_b, r, out, kind == kSmallmExact, st);
     }
     return smallm::run(dx, act, m, *w, bias, lora_a, lora_b, r, out, workspace, workspace_bytes, st);
   }

@@ -44,6 +44,7 @@ namespace sb {
 namespace lut {
 
 constexpr int kThreads = 256, kWarps = 8;
+constexpr int kTableBytes = 256 * 128;    // per-lane byte -> half2 table (lookup mode)
 constexpr int kGroup = 4;                 // 64-blocks per load group (one absmax word per row)
 constexpr int kMaxSplits = 8;             // cluster size along the reduction (portable)
 constexpr int64_t kMaxReduction = 9216;   // longest reduction on this path (its error grows as sqrt)
@@ -55,7 +56,7 @@ constexpr int64_t kMaxReduction = 9216;   // longest reduction on this path (its
 constexpr float kAlpha = 1.3661651611328125f;
 constexpr float kInvAlpha = 1.0f / 1.3661651611328125f;
 
-// Per-lane byte -> half2 table (32 KB, static so its base folds into the loads).
+// Per-lane byte -> half2 table (32 KB of shared memory).
 __device__ __forceinline__ void build_table(uint32_t* table) {
   for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) {
     const int e = i >> 3, part = i & 7;
@@ -94,6 +95,26 @@ __device__ __forceinline__ void mma16816_z(float (&d)[4], const uint32_t (&a)[4]
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
+// The block table of the exact mode: lane t of a quad computes entries 4t .. 4t + 3
+// as fp16(NF4[i] * scale) (one rounding of the fp32 product, as the reference
+// decoder) and splits them into the low- and high-byte words nf4_expand8 reads;
+// three shuffles per word gather the other lanes' quarters.
+__device__ __forceinline__ void quad_table(float scale, const float (&nf4q)[4], int t, uint32_t (&L)[4],
+                                           uint32_t (&H)[4]) {
+  const __half2 h01 = __floats2half2_rn(__fmul_rn(nf4q[0], scale), __fmul_rn(nf4q[1], scale));
+  const __half2 h23 = __floats2half2_rn(__fmul_rn(nf4q[2], scale), __fmul_rn(nf4q[3], scale));
+  const uint32_t u01 = *reinterpret_cast<const uint32_t*>(&h01);
+  const uint32_t u23 = *reinterpret_cast<const uint32_t*>(&h23);
+  const uint32_t lw = gemm::prmt(u01, u23, 0x6420u), hw = gemm::prmt(u01, u23, 0x7531u);
+  const int base = (threadIdx.x & 31) & ~3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    L[q] = __shfl_sync(0xffffffffu, lw, base + q);
+    H[q] = __shfl_sync(0xffffffffu, hw, base + q);
+  }
+  (void)t;
+}
+
 struct FwdArgs {
   const __half* x;        // [M, K] row-major
   int M;
@@ -123,12 +144,22 @@ struct FwdSmem {
   static constexpr int kRedBytes = kWarps * 16 * 16 * 4;    // per-warp C fragments (aliases the tile)
   static constexpr int kPartBytes = kWarps * 16 * 16 * 4;   // CTA partial [rows <= 128][16]
   __host__ __device__ static size_t tile_bytes(int kb) { return x_bytes(kb) > kRedBytes ? x_bytes(kb) : kRedBytes; }
-  __host__ __device__ static size_t bytes(int kb) { return tile_bytes(kb) + 1024 + kPartBytes; }
+  __host__ __device__ static size_t bytes(int kb, bool exact) {
+    return tile_bytes(kb) + 1024 + kPartBytes + (exact ? 0 : kTableBytes);
+  }
+  // Largest reduction slice per CTA (64-blocks): keeps two CTAs per SM.
+  __host__ __device__ static int kb_max(bool exact) { return NT == 1 ? 64 : (exact ? 40 : 32); }
 };
 
-template <int NT>
+// EXACT = false: the unscaled-codebook table above (fp32 block scales after the
+// MMAs).  EXACT = true: each block's operand values are the reference decoder's
+// fp16(NF4[i] * scale) -- the four lanes of a quad each build a quarter of the
+// block's 16-entry table (four products rounded once) and exchange them by
+// shuffles, then every packed word is expanded through the table with byte
+// permutes (nf4_expand8, as in the tcgen05 kernels); the MMAs then accumulate
+// the decoded weights directly.  The exact mode has no reduction-length limit.
+template <int NT, bool EXACT>
 __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
-  __shared__ __align__(128) uint32_t table[256 * 32];
   extern __shared__ __align__(128) uint8_t dsm[];
   using S = FwdSmem<NT>;
   // Register ring of load groups: three slots (two groups in flight) for 8 token
@@ -149,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   float* red = reinterpret_cast<float*>(dsm);  // reused once every warp is past the tile
   float* code2_s = reinterpret_cast<float*>(dsm + S::tile_bytes(a.kb_split));
   float* part = code2_s + 256;
+  uint32_t* table = reinterpret_cast<uint32_t*>(part + kWarps * 256);  // lookup mode only
 
   // Activation tile [8 NT tokens][kb_cta * 64] (zero rows past M) by cp.async.
   {
@@ -162,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
     lora::cp_async_commit();
   }
   for (int i = tid; i < 256; i += kThreads) code2_s[i] = __ldg(a.code2 + i);
-  build_table(table);
+  if constexpr (!EXACT) build_table(table);
   const float off = __ldg(a.offset);
 
   // This warp's row tile and k-run.
@@ -222,6 +254,9 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   }
   const float soff = off;
   const uint32_t tb = smem_addr(table) + lane4;
+  float nf4q[4];  // code values 4t .. 4t + 3 (the quarter of a block table this lane builds)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) nf4q[i] = c_nf4_values[4 * t + i];
   const uint32_t c2s = smem_addr(code2_s);
 
   for (int G = 0; G < ng; G += kSlots) {
@@ -233,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
 #pragma unroll
         for (int b = 0; b < kGroup; ++b) {
           const uint32_t blk = static_cast<uint32_t>(gi * kGroup + b);
-          const float s_g = ok_g ? __fmul_rn(__fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][0] >> (8 * b)) & 0xFFu) * 4), a2[sl][0]), soff), kInvAlpha) : 0.0f;
-          const float s_g8 = ok_g8 ? __fmul_rn(__fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][1] >> (8 * b)) & 0xFFu) * 4), a2[sl][1]), soff), kInvAlpha) : 0.0f;
+          const float sc_g = ok_g ? __fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][0] >> (8 * b)) & 0xFFu) * 4), a2[sl][0]), soff) : 0.0f;
+          const float sc_g8 = ok_g8 ? __fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][1] >> (8 * b)) & 0xFFu) * 4), a2[sl][1]), soff) : 0.0f;
           // Activation B fragments (rows past M are zero in the tile).
           uint32_t xf[NT][8];
 #pragma unroll
@@ -245,34 +280,59 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
             asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                          : "=r"(xf[nt][4]), "=r"(xf[nt][5]), "=r"(xf[nt][6]), "=r"(xf[nt][7]) : "r"(addr + 16));
           }
-          float ct[NT][4];
           const uint32_t wg[2] = {pk[sl][b][0].x, pk[sl][b][0].y}, wg8[2] = {pk[sl][b][1].x, pk[sl][b][1].y};
+          if constexpr (EXACT) {
+            uint32_t Lg[4], Hg[4], L8[4], H8[4];
+            quad_table(sc_g, nf4q, t, Lg, Hg);
+            quad_table(sc_g8, nf4q, t, L8, H8);
+            uint4 eg[2], e8[2];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t af[4];
-            if ((j & 1) == 0) {
-              af[0] = lookup<0>(tb, wg[j >> 1]);
-              af[1] = lookup<0>(tb, wg8[j >> 1]);
-              af[2] = lookup<1>(tb, wg[j >> 1]);
-              af[3] = lookup<1>(tb, wg8[j >> 1]);
-            } else {
-              af[0] = lookup<2>(tb, wg[j >> 1]);
-              af[1] = lookup<2>(tb, wg8[j >> 1]);
-              af[2] = lookup<3>(tb, wg[j >> 1]);
-              af[3] = lookup<3>(tb, wg8[j >> 1]);
+            for (int h = 0; h < 2; ++h) {
+              eg[h] = gemm::nf4_expand8(wg[h], Lg, Hg);
+              e8[h] = gemm::nf4_expand8(wg8[h], L8, H8);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4& A = eg[j >> 1];
+              const uint4& B8 = e8[j >> 1];
+              uint32_t af[4];
+              af[0] = (j & 1) ? A.z : A.x;
+              af[1] = (j & 1) ? B8.z : B8.x;
+              af[2] = (j & 1) ? A.w : A.y;
+              af[3] = (j & 1) ? B8.w : B8.y;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) lora::mma16816(acc[nt], af, xf[nt][2 * j], xf[nt][2 * j + 1]);
+            }
+          } else {
+            const float s_g = __fmul_rn(sc_g, kInvAlpha), s_g8 = __fmul_rn(sc_g8, kInvAlpha);
+            float ct[NT][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t af[4];
+              if ((j & 1) == 0) {
+                af[0] = lookup<0>(tb, wg[j >> 1]);
+                af[1] = lookup<0>(tb, wg8[j >> 1]);
+                af[2] = lookup<1>(tb, wg[j >> 1]);
+                af[3] = lookup<1>(tb, wg8[j >> 1]);
+              } else {
+                af[0] = lookup<2>(tb, wg[j >> 1]);
+                af[1] = lookup<2>(tb, wg8[j >> 1]);
+                af[2] = lookup<3>(tb, wg[j >> 1]);
+                af[3] = lookup<3>(tb, wg8[j >> 1]);
+              }
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                if (j == 0) mma16816_z(ct[nt], af, xf[nt][0], xf[nt][1]);
+                else lora::mma16816(ct[nt], af, xf[nt][2 * j], xf[nt][2 * j + 1]);
+              }
             }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              if (j == 0) mma16816_z(ct[nt], af, xf[nt][0], xf[nt][1]);
-              else lora::mma16816(ct[nt], af, xf[nt][2 * j], xf[nt][2 * j + 1]);
+              acc[nt][0] = fmaf(s_g, ct[nt][0], acc[nt][0]);
+              acc[nt][1] = fmaf(s_g, ct[nt][1], acc[nt][1]);
+              acc[nt][2] = fmaf(s_g8, ct[nt][2], acc[nt][2]);
+              acc[nt][3] = fmaf(s_g8, ct[nt][3], acc[nt][3]);
             }
-          }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            acc[nt][0] = fmaf(s_g, ct[nt][0], acc[nt][0]);
-            acc[nt][1] = fmaf(s_g, ct[nt][1], acc[nt][1]);
-            acc[nt][2] = fmaf(s_g8, ct[nt][2], acc[nt][2]);
-            acc[nt][3] = fmaf(s_g8, ct[nt][3], acc[nt][3]);
           }
         }
       }
@@ -344,10 +404,10 @@ inline int fwd_slots(int nt) {
   return 2 * device_sm_count();
 }
 
-inline FwdPlan fwd_plan(int64_t m, int64_t n, int64_t k) {
+inline FwdPlan fwd_plan(int64_t m, int64_t n, int64_t k, bool exact) {
   FwdPlan best{};
   best.nt = m <= 8 ? 1 : 2;
-  const int kb_max = best.nt == 1 ? 64 : 32;
+  const int kb_max = best.nt == 1 ? FwdSmem<1>::kb_max(exact) : FwdSmem<2>::kb_max(exact);
   const int64_t kblocks = k / 64, row_tiles = (n + 15) / 16;
   const int slots = fwd_slots(best.nt);
   double best_cost = 1e30;
@@ -373,16 +433,18 @@ inline FwdPlan fwd_plan(int64_t m, int64_t n, int64_t k) {
       }
     }
   }
-  best.smem = best.nt == 1 ? FwdSmem<1>::bytes(best.kb_split) : FwdSmem<2>::bytes(best.kb_split);
+  best.smem = best.nt == 1 ? FwdSmem<1>::bytes(best.kb_split, exact) : FwdSmem<2>::bytes(best.kb_split, exact);
   return best;
 }
 
-inline bool fwd_ok(int64_t m, int64_t n, int64_t k) {
-  return m >= 1 && m <= 16 && k % (64 * kGroup) == 0 && k <= kMaxReduction &&
-         n * (k / 2) < (int64_t(1) << 32);
+inline bool fwd_ok(int64_t m, int64_t n, int64_t k, bool exact) {
+  if (m < 1 || m > 16 || k % (64 * kGroup) != 0 || n * (k / 2) >= (int64_t(1) << 32)) return false;
+  if (!exact && k > kMaxReduction) return false;
+  const int kb_max = m <= 8 ? FwdSmem<1>::kb_max(exact) : FwdSmem<2>::kb_max(exact);
+  return k / 64 <= static_cast<int64_t>(kMaxSplits) * kb_max;
 }
 
-template <int NT>
+template <int NT, bool EXACT>
 inline int launch_fwd(const FwdPlan& pl, const FwdArgs& a, cudaStream_t st) {
   static std::mutex mu;
   static bool configured[64] = {false};
@@ -391,8 +453,8 @@ inline int launch_fwd(const FwdPlan& pl, const FwdArgs& a, cudaStream_t st) {
   {
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(lut_fwd_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(FwdSmem<NT>::bytes(NT == 1 ? 64 : 32)));
+      cudaError_t e = cudaFuncSetAttribute(lut_fwd_kernel<NT, EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(FwdSmem<NT>::bytes(FwdSmem<NT>::kb_max(EXACT), EXACT)));
       if (e != cudaSuccess) return fail(SB_ECUDA, std::string("lut fwd smem attribute: ") + cudaGetErrorString(e));
       configured[dev] = true;
     }
@@ -409,15 +471,16 @@ inline int launch_fwd(const FwdPlan& pl, const FwdArgs& a, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, lut_fwd_kernel<NT>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lut_fwd_kernel<NT, EXACT>, a);
   if (e != cudaSuccess) return fail(SB_ECUDA, std::string("lut_fwd_kernel launch: ") + cudaGetErrorString(e));
   count_launch();
   return check_launch("lut_fwd_kernel");
 }
 
 inline int run_fwd(const uint16_t* act, int64_t m, const sb_nf4_weight& w, const uint16_t* bias,
-                   const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* out, cudaStream_t st) {
-  const FwdPlan pl = fwd_plan(m, w.n_out, w.k_in);
+                   const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* out, bool exact,
+                   cudaStream_t st) {
+  const FwdPlan pl = fwd_plan(m, w.n_out, w.k_in, exact);
   FwdArgs a{};
   a.x = reinterpret_cast<const __half*>(act);
   a.M = static_cast<int>(m);
@@ -437,7 +500,8 @@ inline int run_fwd(const uint16_t* act, int64_t m, const sb_nf4_weight& w, const
   a.lb = reinterpret_cast<const __half*>(lora_b);
   a.r = r;
   a.y = reinterpret_cast<__half*>(out);
-  return pl.nt == 1 ? launch_fwd<1>(pl, a, st) : launch_fwd<2>(pl, a, st);
+  if (exact) return pl.nt == 1 ? launch_fwd<1, true>(pl, a, st) : launch_fwd<2, true>(pl, a, st);
+  return pl.nt == 1 ? launch_fwd<1, false>(pl, a, st) : launch_fwd<2, false>(pl, a, st);
 }
 
 }  // namespace lut

@@ -1,9 +1,10 @@
-"""Both small-M (M <= 16) NF4 kernels against the float64 product of the decoded weight.
+"""The small-M (M <= 16) NF4 forward kernels against the float64 product of the decoded weight.
 
-The table-lookup kernel (the default, nf4_lut.cuh) multiplies fp16(NF4[code]) on
-the tensor cores and applies each 64-block's scale in fp32, so its weight
-rounding differs from the decoder's fp16(NF4[code] * scale); the mma.sync kernel
-(SB_SMALLM=mma, nf4_smallm.cuh) multiplies the decoded weight itself.  Both must
+nf4_lut.cuh in its exact mode (the default) expands every packed word through the
+block's fp16(NF4[code] * scale) table, the reference decoder's values; in its
+lookup mode (SB_SMALLM=lut) it multiplies fp16(alpha * NF4[code]) and applies each
+64-block's scale in fp32, a different weight rounding; the mma.sync kernel
+(SB_SMALLM=mma, nf4_smallm.cuh) multiplies the decoded weight tile.  All must
 pass the GEMM gate of test_gemm_gpu (|a - e| <= 2e-3 + 2e-3 |e|, rel-L2 <= 1e-3)
 against the exact product of the reference decoder's fp16 weight, across the
 work splits the lookup kernel plans: one or several cluster ranks along the
@@ -51,7 +52,7 @@ def _gate(actual, expected):
     assert ok, f"max abs err {max_abs:.3e}, rel-L2 {rel:.3e}"
 
 
-@pytest.mark.parametrize("name", ["lut", "mma"])
+@pytest.mark.parametrize("name", ["exact", "lut", "mma"])
 @pytest.mark.parametrize("m,n,k", [(1, 18944, 3584), (8, 3584, 3584), (9, 512, 3584), (16, 1536, 8960),
                                    (4, 3584, 18944), (2, 200, 128), (13, 48, 64), (16, 4096, 2048)])
 def test_small_m_forward_kernels(kernel, name, m, n, k):
@@ -65,7 +66,7 @@ def test_small_m_forward_kernels(kernel, name, m, n, k):
     assert torch.equal(y, nf4_matmul(x, packed, st))
 
 
-@pytest.mark.parametrize("name", ["lut", "mma"])
+@pytest.mark.parametrize("name", ["exact", "lut", "mma"])
 @pytest.mark.parametrize("m,r", [(1, 16), (12, 64), (7, 8)])
 def test_small_m_forward_lora_bias(kernel, name, m, r):
     from soupsuck_b200.kernels.nf4_gemm import nf4_linear_raw
