@@ -121,7 +121,8 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
 }
 
 // ----------------------------------------------------------------- 2-SM pair launch
-constexpr int kPairStages = 6;
+constexpr int kPairStages = 6;         // dX, and the stream-K forward
+constexpr int kPairFwdTileStages = 4;  // whole-tile forward (leaves room for store staging)
 
 template <int BMODE, int EMODE, int STAGES, bool SK>
 inline int configure_pair(const char* name) {
@@ -169,10 +170,10 @@ inline int pair_slots() {
     if (cached[dev] > 0) return cached[dev];
   }
   int n = 0;
-  if (configure_pair<kNF4Fwd, kStoreF16, kPairStages, false>("nf4_pair_fwd") == SB_OK) {
+  if (configure_pair<kNF4Fwd, kStoreF16, kPairFwdTileStages, false>("nf4_pair_fwd") == SB_OK) {
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = pair_config<kNF4Fwd, kStoreF16, kPairStages>(2, nullptr, attr);
-    if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairStages, false>, &cfg) !=
+    cudaLaunchConfig_t cfg = pair_config<kNF4Fwd, kStoreF16, kPairFwdTileStages>(2, nullptr, attr);
+    if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairFwdTileStages, false>, &cfg) !=
         cudaSuccess) {
       cudaGetLastError();
       n = 0;
@@ -349,7 +350,10 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
       if (rc) return rc;
     }
     if (!dx) {
-      return launch_pair<kNF4Fwd, kStoreF16, kPairStages>(ta, tb, tla, tlb, ty, p, pl.grid, stream, "nf4_pair_fwd");
+      return p.streamk
+          ? launch_pair_sk<kNF4Fwd, kStoreF16, kPairStages, true>(ta, tb, tla, tlb, ty, p, pl.grid, stream, "nf4_pair_fwd")
+          : launch_pair_sk<kNF4Fwd, kStoreF16, kPairFwdTileStages, false>(ta, tb, tla, tlb, ty, p, pl.grid, stream,
+                                                                          "nf4_pair_fwd");
     }
     return launch_pair<kNF4Dx, kStoreF16, kPairStages>(ta, tb, tla, tlb, ty, p, pl.grid, stream, "nf4_pair_dx");
   }
