@@ -659,7 +659,9 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
             nf4_decode_words(w0, w1, b_s + gtid * 128, gtid, scale, valid);
           } else {
             const int r = gtid >> 1, j = gtid & 1;
-            nf4_decode_words(w0, w1, b_s + j * (kBK * 128) + r * 128, r, scale, valid);
+            // Lanes 2r and 2r + 1 write row r of the two panels (8 KB apart, the same
+            // banks): the odd lane writes its chunks in flipped order.
+            nf4_decode_words_flip(w0, w1, b_s + j * (kBK * 128) + r * 128, r, scale, valid, 4u * j);
           }
         }
         fence_proxy_async_smem();

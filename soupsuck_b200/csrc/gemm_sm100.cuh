@@ -163,6 +163,32 @@ __device__ __forceinline__ void nf4_decode_words(uint4 p0, uint4 p1, uint8_t* ds
 }
 
 // Same, reading the packed bytes from shared memory (`raw_lo`: bytes 0-15, `raw_hi`: 16-31).
+// nf4_decode_words with the chunk order of the row flipped by `flip` (0 or 4):
+// chunk c of the row is written by store c ^ flip.  Two lanes that write the same
+// row index of two panels 8 KB apart (same banks) then never hit the same
+// 16-byte bank group in one store instruction when their flips differ.
+__device__ __forceinline__ void nf4_decode_words_flip(uint4 p0, uint4 p1, uint8_t* dst, int r, float scale,
+                                                      bool valid, uint32_t flip) {
+  const uint32_t swz = static_cast<uint32_t>(r & 7) ^ flip;
+  if (!valid) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      *reinterpret_cast<uint4*>(dst + ((c ^ swz) << 4)) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  uint32_t L[4], H[4];
+  nf4_table(scale, L, H);
+  const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+  const bool f = flip != 0;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    // Store c writes chunk c ^ flip, whose codes are words[c ^ flip].
+    const uint32_t w = f ? words[c ^ 4] : words[c];
+    *reinterpret_cast<uint4*>(dst + ((c ^ swz) << 4)) = nf4_expand8(w, L, H);
+  }
+}
+
 __device__ __forceinline__ void nf4_decode_row(const uint8_t* raw_lo, const uint8_t* raw_hi,
                                                uint8_t* dst, int r, float scale, bool valid) {
   const uint4 p0 = valid ? *reinterpret_cast<const uint4*>(raw_lo) : make_uint4(0, 0, 0, 0);
