@@ -163,6 +163,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int er
   }
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// Wait until the preceding kernel of the stream (launched before this one with
+// programmatic stream serialisation allowed) has completed and its memory
+// operations are visible; a no-op for an ordinary launch.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel of the stream be scheduled once every CTA of this grid has
+// reached this point (it still waits for this grid's completion before touching
+// memory).
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---------------------------------------------------------------- TMA loads
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -153,8 +153,12 @@ inline cudaLaunchConfig_t pair_config(int grid, cudaStream_t stream, cudaLaunchA
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: the kernel's set-up may overlap the previous
+  // kernel of the stream (it waits for it before touching global memory).
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cfg;
 }
 
@@ -171,7 +175,7 @@ inline int pair_slots() {
   }
   int n = 0;
   if (configure_pair<kNF4Fwd, kStoreF16, kPairFwdTileStages, false>("nf4_pair_fwd") == SB_OK) {
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = pair_config<kNF4Fwd, kStoreF16, kPairFwdTileStages>(2, nullptr, attr);
     if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairFwdTileStages, false>, &cfg) !=
         cudaSuccess) {
@@ -190,7 +194,7 @@ int launch_pair_sk(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap
                    const CUtensorMap& y, Params p, int grid, cudaStream_t stream, const char* name) {
   if (int rc = configure_pair<BMODE, EMODE, STAGES, SK>(name)) return rc;
   if (grid <= 0) return SB_OK;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pair_config<BMODE, EMODE, STAGES>(grid, stream, attr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, pair::pair_kernel<BMODE, EMODE, STAGES, SK>, a, b, la, lb, y, p);
   if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " launch: " + cudaGetErrorString(e));

@@ -427,13 +427,19 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
     *last_flag = 0;
     fence_barrier_init();
   }
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) code2_s[i] = __ldg(p.code2 + i);
   if (warp == 1) tmem_alloc_pair(tmem_holder, C::kTmemCols);
   tc_fence_before();
   // Barrier initialisation and the TMEM address must be visible to both CTAs
   // before any thread signals the peer.
   cluster_sync_all();
   tc_fence_after();
+  // Launched with programmatic stream serialisation: the set-up above overlaps
+  // the previous kernel of the stream; no global memory is read or written
+  // before that kernel has completed and its writes are visible.
+  grid_dependency_wait();
+  launch_dependents();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) code2_s[i] = __ldg(p.code2 + i);
+  __syncthreads();
   const uint32_t tmem_base = *tmem_holder;
   const int rows_valid = runtime_rows(p);
   // rank 0's barriers, as shared::cluster addresses (stride 8 bytes per barrier)
