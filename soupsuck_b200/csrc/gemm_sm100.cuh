@@ -439,7 +439,8 @@ template <int EMODE, int MSUB, int BN>
 __device__ __forceinline__ void run_epilogue_role(const Params& p, uint32_t tmem_base, uint64_t* acc_full,
                                                   uint64_t* acc_empty, uint64_t* epi_mb,
                                                   volatile int* abort_flag, volatile int* last_flag,
-                                                  int warp, int lane, int num_tiles, int rows_valid) {
+                                                  int warp, int lane, int num_tiles, int rows_valid,
+                                                  int m_tiles) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int etid = (warp - 4) * 32 + lane;
@@ -449,7 +450,7 @@ __device__ __forceinline__ void run_epilogue_role(const Params& p, uint32_t tmem
     UnitIter iter(p, num_tiles);
     Unit u;
     while (iter.next(u)) {
-      const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
+      const int mt = u.tile % m_tiles, nt = u.tile / m_tiles;
       const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
       if (m0 >= rows_valid) continue;
       const int buf = tl & 1;
@@ -593,7 +594,6 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.m_tiles * p.n_tiles;
   const bool has_lora = p.lora_r > 0;
 
   if (threadIdx.x == 0) {
@@ -623,6 +623,11 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int rows_valid = runtime_rows(p);
+  // Tiles past the runtime row count (the CE backward's compacted labelled rows,
+  // a count known only on the device) are left out of the schedule, so the
+  // valid tiles are shared evenly by the CTAs.
+  const int m_tiles = min(p.m_tiles, (rows_valid + MSUB * kTileRows - 1) / (MSUB * kTileRows));
+  const int num_tiles = m_tiles * p.n_tiles;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -638,7 +643,7 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
       UnitIter iter(p, num_tiles);
       Unit u;
       while (ok && iter.next(u)) {
-        const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
+        const int mt = u.tile % m_tiles, nt = u.tile / m_tiles;
         const int m0 = mt * MSUB * kTileRows, n0 = nt * BN;
         if (m0 >= rows_valid) continue;
         const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
@@ -694,7 +699,7 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
       UnitIter iter(p, num_tiles);
       Unit u;
       while (ok && iter.next(u)) {
-        if ((u.tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
+        if ((u.tile % m_tiles) * MSUB * kTileRows >= rows_valid) continue;
         const int buf = tl & 1;
         const uint32_t aph = (tl >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag)) { ok = false; break; }
@@ -750,7 +755,7 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
     }
   } else if (warp >= 4 && warp < 8) {
     run_epilogue_role<EMODE, MSUB, BN>(p, tmem_base, acc_full, acc_empty, epi_mb, abort_flag, last_flag,
-                                       warp, lane, num_tiles, rows_valid);
+                                       warp, lane, num_tiles, rows_valid, m_tiles);
   } else if (C::kNF4 && warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders
     // Group g decodes the k-steps whose global index has parity g.  Each thread
@@ -780,8 +785,8 @@ __global__ void __launch_bounds__(Cfg<BMODE, MSUB, BN, STAGES>::kThreads, 1)
     UnitIter iter(p, num_tiles);
     Unit u;
     while (ok && iter.next(u)) {
-      if ((u.tile % p.m_tiles) * MSUB * kTileRows >= rows_valid) continue;
-      const int n0 = (u.tile / p.m_tiles) * BN;
+      if ((u.tile % m_tiles) * MSUB * kTileRows >= rows_valid) continue;
+      const int n0 = (u.tile / m_tiles) * BN;
       const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
       // First k-step of this unit owned by this group.
       const int first = u.k0 + ((static_cast<int>(it & 1) == group) ? 0 : 1);
