@@ -236,17 +236,26 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, EpiState& st, co
                                                int row, int col0, int rows_valid) {
   if constexpr (EMODE == kCeStats) {
     // Logits are the fp16-rounded GEMM result (reference: torch.mm with fp16 output,
-    // solution/kernels/cross_entropy.py:149); statistics follow :57-89.
+    // solution/kernels/cross_entropy.py:149); statistics follow :57-89.  Columns
+    // past N only occur in a launch's last chunk, which takes the guarded path.
     float z[32];
+    const bool full = col0 + 32 <= p.N;
+    if (full) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) z[j] = (col0 + j < p.N) ? round_f16(__uint_as_float(v[j])) : -INFINITY;
-    float cmax = z[0];
-    int carg = 0;
+      for (int j = 0; j < 32; ++j) z[j] = round_f16(__uint_as_float(v[j]));
+    } else {
 #pragma unroll
-    for (int j = 1; j < 32; ++j) {
-      if (z[j] > cmax) { cmax = z[j]; carg = j; }
+      for (int j = 0; j < 32; ++j) z[j] = (col0 + j < p.N) ? round_f16(__uint_as_float(v[j])) : -INFINITY;
     }
+    float mx[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx[j] = fmaxf(fmaxf(z[4 * j], z[4 * j + 1]), fmaxf(z[4 * j + 2], z[4 * j + 3]));
+    const float cmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
     if (cmax > st.m) {
+      // A new running maximum: rescale the sums and record its first column.
+      int carg = 31;
+#pragma unroll
+      for (int j = 31; j >= 0; --j) carg = (z[j] == cmax) ? j : carg;
       const float r = st.m == -INFINITY ? 0.0f : __expf(st.m - cmax);
       st.s *= r;
       st.t *= r;
@@ -254,12 +263,25 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, EpiState& st, co
       st.arg = col0 + carg;
     }
     if (st.m != -INFINITY) {
+      if (full) {
+        // Four independent partial sums per thread (short dependency chains).
+        float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f}, t4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (col0 + j < p.N) {
+        for (int j = 0; j < 32; ++j) {
           const float e = __expf(z[j] - st.m);
-          st.s += e;
-          st.t = fmaf(e, z[j], st.t);
+          s4[j & 3] += e;
+          t4[j & 3] = fmaf(e, z[j], t4[j & 3]);
+        }
+        st.s += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        st.t += (t4[0] + t4[1]) + (t4[2] + t4[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (col0 + j < p.N) {
+            const float e = __expf(z[j] - st.m);
+            st.s += e;
+            st.t = fmaf(e, z[j], st.t);
+          }
         }
       }
     }
@@ -276,10 +298,11 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, EpiState& st, co
     __half* out = static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo;
     const int64_t g0 = p.col_offset + col0;
     float d[32];
+    const bool has_tgt = st.tgt >= g0 && st.tgt < g0 + 32;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       float e = __expf(round_f16(__uint_as_float(v[j])) - st.lse);
-      if (g0 + j == st.tgt) e -= 1.0f;
+      if (has_tgt && g0 + j == st.tgt) e -= 1.0f;
       d[j] = e * st.gscale;
     }
     if (p.vec_ok && col0 + 32 <= p.N) {
