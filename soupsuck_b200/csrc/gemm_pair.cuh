@@ -333,29 +333,18 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
 #pragma unroll
           for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
           const int64_t off = static_cast<int64_t>(c * 8) * 128 + etid;
-          for (int cc = c_lo; cc <= c_hi; cc += 2) {
-            float4 x[2][8];
+          for (int ci = c_lo; ci <= c_hi; ++ci) {
+            const int64_t first_tile = (total * ci / pairs) / p.k_blocks;
+            const int cslot = first_tile == u.tile ? 0 : 1;
+            const float4* src = reinterpret_cast<const float4*>(p.partials) +
+                                ((static_cast<int64_t>(ci) * 2 + rank) * 2 + cslot) * kSlotF4 + off;
+            float4 x[8];
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-              const int ci = cc + b;
-              if (ci <= c_hi) {
-                const int64_t first_tile = (total * ci / pairs) / p.k_blocks;
-                const int cslot = first_tile == u.tile ? 0 : 1;
-                const float4* src = reinterpret_cast<const float4*>(p.partials) +
-                                    ((static_cast<int64_t>(ci) * 2 + rank) * 2 + cslot) * kSlotF4 + off;
+            for (int j = 0; j < 8; ++j) x[j] = __ldcg(src + j * 128);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) x[b][j] = __ldcg(src + j * 128);
-              }
-            }
-#pragma unroll
-            for (int b = 0; b < 2; ++b) {
-              if (cc + b <= c_hi) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  sum[4 * j] += x[b][j].x; sum[4 * j + 1] += x[b][j].y;
-                  sum[4 * j + 2] += x[b][j].z; sum[4 * j + 3] += x[b][j].w;
-                }
-              }
+            for (int j = 0; j < 8; ++j) {
+              sum[4 * j] += x[j].x; sum[4 * j + 1] += x[j].y;
+              sum[4 * j + 2] += x[j].z; sum[4 * j + 3] += x[j].w;
             }
           }
           uint32_t v[32];
