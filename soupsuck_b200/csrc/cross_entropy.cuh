@@ -85,6 +85,77 @@ __global__ void ce_merge_kernel(const float* __restrict__ stats, const int* __re
   if (row_max) row_max[i] = M;
 }
 
+// The same merge spread over a CTA: 32 consecutive rows (one per lane) and 16
+// warps; warp w folds tiles w, w + 16, ... in increasing order (loads coalesced
+// across the rows), then warp 0 merges the 16 partial results in warp order.
+// On equal maxima the smaller column wins, as in the tile-order scan above, so
+// the first argmax is kept; the order is fixed, so results are deterministic.
+constexpr int kMergeWarps = 16;
+
+__device__ __forceinline__ void merge_stat(float& M, float& S, float& T, int& A, float m2, float s2, float t2,
+                                           int a2) {
+  if (m2 == -INFINITY) return;
+  if (M == -INFINITY) {
+    M = m2; S = s2; T = t2; A = a2;
+    return;
+  }
+  if (m2 > M) {
+    const float r = __expf(M - m2);
+    S = fmaf(S, r, s2);
+    T = fmaf(T, r, t2);
+    M = m2;
+    A = a2;
+  } else {
+    const float r = __expf(m2 - M);
+    S = fmaf(s2, r, S);
+    T = fmaf(t2, r, T);
+    if (m2 == M && a2 < A) A = a2;
+  }
+}
+
+__global__ void __launch_bounds__(32 * kMergeWarps) ce_merge2_kernel(
+    const float* __restrict__ stats, const int* __restrict__ args, int64_t ld, int n_tiles,
+    const int64_t* __restrict__ targets, int64_t ignore, int64_t rows, float* __restrict__ loss,
+    float* __restrict__ entropy, int64_t* __restrict__ argmax, float* __restrict__ lse_out,
+    float* __restrict__ row_max) {
+  __shared__ float part[kMergeWarps][4][32];
+  __shared__ int part_arg[kMergeWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  const bool ok = i < rows;
+  float M = -INFINITY, S = 0.0f, T = 0.0f, tz = 0.0f;
+  int A = 0x7fffffff;
+  if (ok) {
+    for (int nt = warp; nt < n_tiles; nt += kMergeWarps) {
+      const float* b = stats + static_cast<int64_t>(nt) * 4 * ld + i;
+      const float mt = b[0], st = b[ld], tt = b[2 * ld];
+      tz += b[3 * ld];
+      merge_stat(M, S, T, A, mt, st, tt, args[static_cast<int64_t>(nt) * ld + i]);
+    }
+  }
+  part[warp][0][lane] = M;
+  part[warp][1][lane] = S;
+  part[warp][2][lane] = T;
+  part[warp][3][lane] = tz;
+  part_arg[warp][lane] = A;
+  __syncthreads();
+  if (warp != 0 || !ok) return;
+  M = part[0][0][lane]; S = part[0][1][lane]; T = part[0][2][lane]; tz = part[0][3][lane];
+  A = part_arg[0][lane];
+#pragma unroll 1
+  for (int w = 1; w < kMergeWarps; ++w) {
+    merge_stat(M, S, T, A, part[w][0][lane], part[w][1][lane], part[w][2][lane], part_arg[w][lane]);
+    tz += part[w][3][lane];
+  }
+  const float l = M + logf(S);
+  lse_out[i] = l;
+  entropy[i] = l - T / S;
+  const int64_t tg = targets[i];
+  loss[i] = tg != ignore ? l - tz : 0.0f;
+  argmax[i] = M == -INFINITY ? 0 : A;
+  if (row_max) row_max[i] = M;
+}
+
 // Single-block stream compaction of labelled rows (deterministic order).
 __global__ void __launch_bounds__(1024) ce_compact_kernel(const int64_t* __restrict__ targets,
                                                           int64_t n, int64_t ignore,
@@ -258,10 +329,10 @@ static int ce_forward_impl(const uint16_t* hidden, int64_t t, int64_t h, const u
   p.col_offset = 0;
   rc = launch<kDenseK, kCeStats, 1, sb::ce::kFwdBN, 4>(ta, tb, ta, ta, p, st, "ce_logits_stats");
   if (rc) return rc;
-  sb::ce::ce_merge_kernel<<<static_cast<unsigned>((t + 255) / 256), 256, 0, st>>>(
+  sb::ce::ce_merge2_kernel<<<static_cast<unsigned>((t + 31) / 32), 32 * sb::ce::kMergeWarps, 0, st>>>(
       stats, args, t, n_tiles, targets, ignore_index, t, loss, entropy, argmax, lse, row_max);
   sb::count_launch();
-  return sb::check_launch("ce_merge_kernel");
+  return sb::check_launch("ce_merge2_kernel");
 }
 
 int sb_ce_forward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t* weight, int64_t v,
