@@ -215,13 +215,16 @@ __global__ void ce_gather_kernel(const __half* __restrict__ hidden, int64_t h,
   for (int64_t c = threadIdx.x; c < h / 8; c += blockDim.x) d[c] = s[c];
 }
 
-__global__ void ce_finalize_kernel(const float* __restrict__ acc, const float* __restrict__ gain,
-                                   const int* __restrict__ inv, int64_t h, void* __restrict__ out,
-                                   int odt) {
+// dHidden[row] = gain * (acc + acc2)[compacted row]: the two halves of the split
+// dZ . W_chunk reduction are added here, in a fixed order.
+__global__ void ce_finalize_kernel(const float* __restrict__ acc, const float* __restrict__ acc2,
+                                   const float* __restrict__ gain, const int* __restrict__ inv, int64_t h,
+                                   void* __restrict__ out, int odt) {
   const int64_t row = blockIdx.x;
   const int c = inv[row];
   for (int64_t col = threadIdx.x; col < h; col += blockDim.x) {
-    const float v = c < 0 ? 0.0f : acc[static_cast<int64_t>(c) * h + col] * gain[c];
+    const int64_t at = static_cast<int64_t>(c) * h + col;
+    const float v = c < 0 ? 0.0f : (acc[at] + acc2[at]) * gain[c];
     st_from_f32(out, odt, row * h + col, v);
   }
 }
@@ -229,7 +232,7 @@ __global__ void ce_finalize_kernel(const float* __restrict__ acc, const float* _
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct BwdLayout {
-  size_t idx, inv, count, hc, tc, lc, gc, gain, acc, dz, total;
+  size_t idx, inv, count, hc, tc, lc, gc, gain, acc, acc2, dz, total;
 };
 
 inline BwdLayout bwd_layout(int64_t t, int64_t h, int64_t v) {
@@ -246,6 +249,7 @@ inline BwdLayout bwd_layout(int64_t t, int64_t h, int64_t v) {
   L.gc = take(t * 4);
   L.gain = take(t * 4);
   L.acc = take(t * h * 4);
+  L.acc2 = take(t * h * 4);
   L.dz = take(t * chunk * 2);
   L.total = o;
   return L;
@@ -377,6 +381,7 @@ int sb_ce_backward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t*
   float* gc = reinterpret_cast<float*>(ws + L.gc);
   float* gain = reinterpret_cast<float*>(ws + L.gain);
   float* acc = reinterpret_cast<float*>(ws + L.acc);
+  float* acc2 = reinterpret_cast<float*>(ws + L.acc2);
   __half* dz = reinterpret_cast<__half*>(ws + L.dz);
   const int64_t chunk = sb::ce::bwd_chunk(t, v);
 
@@ -387,7 +392,8 @@ int sb_ce_backward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t*
       reinterpret_cast<const __half*>(hidden), h, targets, lse, grad, idx, count, hc, tc, lc, gc, gain);
   sb::count_launch();
   if (int rc = sb::check_launch("ce_gather_kernel")) return rc;
-  cudaError_t e = cudaMemsetAsync(acc, 0, static_cast<size_t>(t) * h * 4, st);
+  // acc and acc2 are adjacent in the workspace (one clear for both).
+  cudaError_t e = cudaMemsetAsync(acc, 0, L.dz - L.acc, st);
   if (e != cudaSuccess) return sb::fail(SB_ECUDA, cudaGetErrorString(e));
 
   CUtensorMap t_hc, t_dz;
@@ -427,16 +433,21 @@ int sb_ce_backward(const uint16_t* hidden, int64_t t, int64_t h, const uint16_t*
     p2.N = static_cast<int>(h);
     p2.K = static_cast<int>(vc);
     p2.m_tiles = static_cast<int>((t + 127) / 128);
-    p2.n_tiles = static_cast<int>((h + 127) / 128);
+    // 128 x 256 tiles with each tile's reduction split in two halves (the second
+    // accumulating into acc2): as many CTAs as 128 x 128 tiles, but UMMAs that
+    // read 12 KB of shared memory per 128 cycles instead of 8 KB per 64.
+    p2.n_tiles = static_cast<int>((h + 255) / 256);
+    p2.ksplit = 2;
+    p2.out_split = acc2;
     p2.k_blocks = static_cast<int>((vc + 63) / 64);
     p2.m_dev = count;
     p2.vec_ok = (h % 4 == 0);
     p2.out = acc;
     p2.ldo = h;
-    rc = launch<kDenseMN, kAccF32, 1, 128, 4>(t_dz, t_wmn, t_dz, t_dz, p2, st, "ce_dz_weight");
+    rc = launch<kDenseMN, kAccF32, 1, 256, 4>(t_dz, t_wmn, t_dz, t_dz, p2, st, "ce_dz_weight");
     if (rc) return rc;
   }
-  sb::ce::ce_finalize_kernel<<<static_cast<unsigned>(t), 256, 0, st>>>(acc, gain, inv, h, dhidden, dh_dtype);
+  sb::ce::ce_finalize_kernel<<<static_cast<unsigned>(t), 256, 0, st>>>(acc, acc2, gain, inv, h, dhidden, dh_dtype);
   sb::count_launch();
   return sb::check_launch("ce_finalize_kernel");
 }

@@ -113,7 +113,8 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
   const int tiles = p.m_tiles * p.n_tiles;
   if (tiles == 0) return SB_OK;
   const int sms = device_sm_count();
-  int grid = tiles < sms ? tiles : sms;
+  const int units = tiles * (p.ksplit > 1 ? p.ksplit : 1);
+  int grid = units < sms ? units : sms;
   if (p.streamk) grid = streamk_grid(tiles, p.k_blocks, sms);
   kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(a, b, la, lb, p);
   count_launch();

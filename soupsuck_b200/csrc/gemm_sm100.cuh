@@ -49,6 +49,9 @@ struct Params {
   int vec_ok;             // output rows are 16-byte aligned
   int store_tma;          // 2-SM pair kernel: fp16 output written by bulk tensor stores
   int streamk;            // 1: stream-K schedule (equal k-iteration shares per CTA)
+  int ksplit;             // whole-tile schedule: 2 splits every tile's reduction in two halves,
+                          // the second half accumulating into out_split (0 or 1: no split)
+  void* out_split;        // kAccF32 / kStoreF32 output of the second half
   float* partials;        // stream-K: [grid, 2, MSUB*128, BN] fp32 partial tiles
   int* counters;          // stream-K: [tiles] arrival counters, zero before launch
   // NF4 weight
@@ -212,12 +215,14 @@ struct EpiState {
   int arg;             // CE stats: first argmax (column within this launch)
   int64_t tgt;         // target vocabulary index (or ignore_index)
   float lse, gscale;   // CE dz: row lse and g / gain
+  float* out;          // kStoreF32 / kAccF32: output base (p.out, or p.out_split for a second half)
 };
 
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
 
 template <int EMODE>
 __device__ __forceinline__ void epilogue_begin(const Params& p, EpiState& st, int row, int rows_valid) {
+  st.out = static_cast<float*>(p.out);
   if constexpr (EMODE == kCeStats) {
     st.m = -INFINITY; st.s = 0.0f; st.t = 0.0f; st.tz = 0.0f; st.arg = 0x7fffffff;
     st.tgt = row < rows_valid ? p.targets[row] : p.ignore_index;
@@ -349,7 +354,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, EpiState& st, co
     }
   } else {  // kStoreF32 / kAccF32
     if (row >= rows_valid) return;
-    float* out = static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+    float* out = st.out + static_cast<int64_t>(row) * p.ldo;
     if (p.vec_ok && col0 + 32 <= p.N) {
       float4* dst = reinterpret_cast<float4*>(out + col0);
 #pragma unroll
@@ -397,11 +402,13 @@ __device__ __forceinline__ void epilogue_end(const Params& p, const EpiState& st
 // tile split between CTAs is finished by whichever contributor arrives last.
 struct Unit {
   int tile, k0, k1;
+  int split;  // half of a split reduction (0 without a split)
 };
 
 struct UnitIter {
   int64_t cursor, end;
   int kb, stride;
+  int ks = 1, tiles = 0;
   bool streamk;
   __device__ UnitIter(const Params& p, int num_tiles) : UnitIter(p, num_tiles, blockIdx.x, gridDim.x) {}
   // Worker `id` of `count` (a CTA, or a CTA pair of a 2-SM kernel).
@@ -414,23 +421,27 @@ struct UnitIter {
       end = total * (id + 1) / count;
       stride = 0;
     } else {
+      ks = p.ksplit > 1 ? p.ksplit : 1;
+      tiles = num_tiles;
       cursor = id;
-      end = num_tiles;
+      end = static_cast<int64_t>(num_tiles) * ks;
       stride = count;
     }
   }
   __device__ bool next(Unit& u) {
     if (cursor >= end) return false;
     if (streamk) {
+      u.split = 0;
       u.tile = static_cast<int>(cursor / kb);
       u.k0 = static_cast<int>(cursor % kb);
       const int64_t k1 = u.k0 + (end - cursor);
       u.k1 = static_cast<int>(k1 < kb ? k1 : kb);
       cursor += u.k1 - u.k0;
     } else {
-      u.tile = static_cast<int>(cursor);
-      u.k0 = 0;
-      u.k1 = kb;
+      u.tile = static_cast<int>(cursor % tiles);
+      u.split = static_cast<int>(cursor / tiles);
+      u.k0 = kb * u.split / ks;
+      u.k1 = kb * (u.split + 1) / ks;
       cursor += stride;
     }
     return true;
@@ -481,12 +492,15 @@ __device__ __forceinline__ void run_epilogue_role(const Params& p, uint32_t tmem
       if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * MSUB * BN;
-      if (u.k0 == 0 && u.k1 == p.k_blocks) {
+      // Whole units (every unit of the whole-tile schedule, split or not) run the
+      // epilogue directly; stream-K partial units take the fix-up below.
+      if (!p.streamk || (u.k0 == 0 && u.k1 == p.k_blocks)) {
 #pragma unroll 1
         for (int ms = 0; ms < MSUB; ++ms) {
           const int row = m0 + ms * kTileRows + q * 32 + lane;
           EpiState st;
           epilogue_begin<EMODE>(p, st, row, rows_valid);
+          if (u.split) st.out = static_cast<float*>(p.out_split);
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t v[32];
