@@ -96,26 +96,47 @@ def measured_peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples SM clock and clock-event (throttle) reasons through NVML every
-    10 ms in a background thread while the timed region runs (read-only)."""
+    """Samples the SM clock and the clock-event (throttle) reasons of the GPU the
+    process uses through NVML (read-only): once when the timed region starts,
+    every millisecond from a background thread while it runs, and once when it
+    ends.  The NVML handle is found by the device's UUID (NVML's indices need not
+    match CUDA's under CUDA_VISIBLE_DEVICES), then its PCI bus id, then its index."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
 
-    def __init__(self, index, period=0.01):
+    def __init__(self, index, period=0.001):
         self.index, self.period = index, period
         self.samples, self.max_mhz, self.reasons = [], None, set()
+        self.handle = None
+
+    def _handle(self, pynvml):
+        import torch
+        props = torch.cuda.get_device_properties(self.index)
+        uuid = getattr(props, "uuid", None)
+        if uuid is not None:
+            try:
+                text = str(uuid)
+                return pynvml.nvmlDeviceGetHandleByUUID(text if text.startswith("GPU-") else "GPU-" + text)
+            except Exception:
+                pass
+        try:
+            bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _sample(self):
+        import pynvml
+        self.samples.append(pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        for name, bit in self.REASONS.items():
+            if mask & bit:
+                self.reasons.add(name)
 
     def _run(self):
-        import pynvml
-        h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
-        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
         while not self.stop.is_set():
-            self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-            mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-            for name, bit in self.REASONS.items():
-                if mask & bit:
-                    self.reasons.add(name)
+            self._sample()
             self.stop.wait(self.period)
 
     def __enter__(self):
@@ -125,6 +146,9 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
+            self.handle = self._handle(pynvml)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self._sample()
             self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
         except Exception:
@@ -135,6 +159,11 @@ class ClockSampler:
         self.stop.set()
         if self.thread is not None:
             self.thread.join(timeout=5)
+        if self.handle is not None:
+            try:
+                self._sample()
+            except Exception:
+                pass
 
     def summary(self):
         if not self.samples:
