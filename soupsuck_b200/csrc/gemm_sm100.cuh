@@ -109,18 +109,19 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
 __device__ __forceinline__ uint4 nf4_expand8(uint32_t w, const uint32_t (&L)[4],
                                              const uint32_t (&H)[4]) {
   uint4 o;
+  // prmt reads only the low 16 bits of its selector, so the selectors of both
+  // halves come from one mask of the whole word (the high half shifted down).
+  const uint32_t s_all = w & 0x77777777u;
+  const uint32_t sel_all = ((w >> 1) & 0x44444444u) | 0x32103210u;
   {
-    const uint32_t s = w & 0x7777u;
-    const uint32_t sel = ((w >> 1) & 0x4444u) | 0x3210u;
+    const uint32_t s = s_all, sel = sel_all;
     const uint32_t lo = prmt(prmt(L[0], L[1], s), prmt(L[2], L[3], s), sel);
     const uint32_t hi = prmt(prmt(H[0], H[1], s), prmt(H[2], H[3], s), sel);
     o.x = prmt(lo, hi, 0x4051u);  // elements 0, 1 (high nibble of byte 0 first)
     o.y = prmt(lo, hi, 0x6273u);  // elements 2, 3
   }
   {
-    const uint32_t u = w >> 16;
-    const uint32_t s = u & 0x7777u;
-    const uint32_t sel = ((u >> 1) & 0x4444u) | 0x3210u;
+    const uint32_t s = s_all >> 16, sel = sel_all >> 16;
     const uint32_t lo = prmt(prmt(L[0], L[1], s), prmt(L[2], L[3], s), sel);
     const uint32_t hi = prmt(prmt(H[0], H[1], s), prmt(H[2], H[3], s), sel);
     o.z = prmt(lo, hi, 0x4051u);

@@ -1,36 +1,36 @@
-// Small-M NF4 linear (M <= 16 activation rows) by table lookup: forward Y = X . deq(W)^T.
+// Small-M NF4 linear (M <= 16 activation rows): forward Y = X . deq(W)^T on mma.sync.
 //
 // At M <= 16 the product is bound by reading the packed weight (0.52 byte per
 // weight), so the limit is how few instructions turn a packed byte into MMA
-// operands.  Here one shared-memory load does it:
+// operands.  Two modes:
 //
-//   * a 256-entry table maps a packed byte (two codes, the earlier element in the
-//     high nibble) to the half2 (NF4[hi], NF4[lo]) of the two UNSCALED code
-//     values.  Every lane has its own copy of the table (entry e of lane l at
-//     byte e * 128 + 4 l), so a warp's 32 lookups hit 32 different banks;
-//   * the block scale s(n, b) = fp32(code2[absmax[n, b]] * absmax2) + offset of
-//     the bitsandbytes format multiplies, in fp32, the partial product of each
-//     64-element block after its four mma.sync.m16n8k16 steps (the scale is
-//     constant inside a block and an MMA never straddles two blocks).
+//   * exact (default): every operand value is the reference decoder's
+//     fp16(NF4[i] * scale).  One lane owns whole 64-blocks: it builds the
+//     block's 16-entry table itself (sixteen fp32 products, each rounded once)
+//     and expands the block's eight packed words through it with byte permutes;
+//   * lookup (SB_SMALLM=lut): a 256-entry table maps a packed byte (two codes,
+//     the earlier element in the high nibble) to the half2 of the two UNSCALED
+//     code values, one shared-memory load per byte.  Every lane has its own copy
+//     of the table (entry e of lane l at byte e * 128 + 4 l), so a warp's 32
+//     lookups hit 32 different banks; the block scale s(n, b) =
+//     fp32(code2[absmax[n, b]] * absmax2) + offset of the bitsandbytes format
+//     multiplies, in fp32, the partial product of each 64-element block after
+//     its four mma.sync.m16n8k16 steps.  The weights then enter the MMA as
+//     fp16(NF4[i]) -- a different rounding of the same product, inside the GEMM
+//     gate up to a reduction of kMaxReduction.
 //
 // The weight is the MMA's A operand (16 weight rows per warp tile) and the
-// activations its B operand (8 or 16 tokens).  Inside a 64-element block,
-// lane t of a quad holds the packed bytes 8t .. 8t + 7 (elements 16t .. 16t + 15)
-// of its two rows; k-step j of the block uses bytes 8t + 2j and 8t + 2j + 1, and
-// the activation fragment is permuted the same way, so each lane reads one 8-byte
-// piece of each row per block straight from global memory (no staging, no
-// decoded tile) and its activations as two 16-byte shared-memory loads.
+// activations its B operand (8 or 16 tokens).  The k order inside each MMA is
+// permuted (the activation fragment the same way), so each lane reads its packed
+// bytes straight from global memory (no staging, no decoded tile): in lookup
+// mode lane t of a quad holds bytes 8t .. 8t + 7 of each block of its two rows,
+// in exact mode all 32 bytes of block t of each group of four.
 //
 // Work split: a CTA of 8 warps covers RW row tiles (16 rows each) x KW k-runs
 // (RW * KW = 8); a cluster of S CTAs along grid.y splits the reduction, and the
 // partial sums are combined in fixed rank order through distributed shared
 // memory, then bias and the LoRA term are added and fp16 rows stored.  One launch,
 // no global scratch, deterministic.
-//
-// Numerics: the weights enter the MMA as fp16(NF4[i]) and the scale is applied in
-// fp32 per block, instead of the reference decoder's fp16(NF4[i] * scale) --
-// a different rounding of the same product, inside the GEMM gate (the standalone
-// decoder stays bit-exact).
 //
 // Reference: bitsandbytes' MatMul4Bit / gemv_4bit small-batch path behind
 // solution/nf4_patch.py:43-125; decode rule solution/kernels/nf4.py:41-59.
@@ -95,26 +95,6 @@ __device__ __forceinline__ void mma16816_z(float (&d)[4], const uint32_t (&a)[4]
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
-// The block table of the exact mode: lane t of a quad computes entries 4t .. 4t + 3
-// as fp16(NF4[i] * scale) (one rounding of the fp32 product, as the reference
-// decoder) and splits them into the low- and high-byte words nf4_expand8 reads;
-// three shuffles per word gather the other lanes' quarters.
-__device__ __forceinline__ void quad_table(float scale, const float (&nf4q)[4], int t, uint32_t (&L)[4],
-                                           uint32_t (&H)[4]) {
-  const __half2 h01 = __floats2half2_rn(__fmul_rn(nf4q[0], scale), __fmul_rn(nf4q[1], scale));
-  const __half2 h23 = __floats2half2_rn(__fmul_rn(nf4q[2], scale), __fmul_rn(nf4q[3], scale));
-  const uint32_t u01 = *reinterpret_cast<const uint32_t*>(&h01);
-  const uint32_t u23 = *reinterpret_cast<const uint32_t*>(&h23);
-  const uint32_t lw = gemm::prmt(u01, u23, 0x6420u), hw = gemm::prmt(u01, u23, 0x7531u);
-  const int base = (threadIdx.x & 31) & ~3;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    L[q] = __shfl_sync(0xffffffffu, lw, base + q);
-    H[q] = __shfl_sync(0xffffffffu, hw, base + q);
-  }
-  (void)t;
-}
-
 struct FwdArgs {
   const __half* x;        // [M, K] row-major
   int M;
@@ -136,16 +116,28 @@ struct FwdArgs {
 
 // Dynamic shared memory of the forward kernel: activation tile, code2 table,
 // per-warp fragments, CTA partial.
+//
+// Activation tile geometry.  Lookup mode: token rows of kb * 128 bytes + 16.
+// Exact mode: each 64-block of a token row takes 144 bytes (128 + 16 of skew)
+// and the row pitch is 64 mod 128, so the eight lanes of a quarter-warp (two
+// tokens x four consecutive blocks) read eight different 16-byte bank groups.
 template <int NT>
 struct FwdSmem {
   static constexpr int kTok = 8 * NT;
-  __host__ __device__ static size_t pitch(int kb) { return static_cast<size_t>(kb) * 128 + 16; }
-  __host__ __device__ static size_t x_bytes(int kb) { return kTok * pitch(kb); }
+  static constexpr int kExactBlockBytes = 144;
+  __host__ __device__ static size_t pitch(int kb, bool exact) {
+    if (!exact) return static_cast<size_t>(kb) * 128 + 16;
+    const size_t p = static_cast<size_t>(kb) * kExactBlockBytes;
+    return p + ((64 + 128 - (p & 127)) & 127);
+  }
+  __host__ __device__ static size_t x_bytes(int kb, bool exact) { return kTok * pitch(kb, exact); }
   static constexpr int kRedBytes = kWarps * 16 * 16 * 4;    // per-warp C fragments (aliases the tile)
   static constexpr int kPartBytes = kWarps * 16 * 16 * 4;   // CTA partial [rows <= 128][16]
-  __host__ __device__ static size_t tile_bytes(int kb) { return x_bytes(kb) > kRedBytes ? x_bytes(kb) : kRedBytes; }
+  __host__ __device__ static size_t tile_bytes(int kb, bool exact) {
+    return x_bytes(kb, exact) > kRedBytes ? x_bytes(kb, exact) : kRedBytes;
+  }
   __host__ __device__ static size_t bytes(int kb, bool exact) {
-    return tile_bytes(kb) + 1024 + kPartBytes + (exact ? 0 : kTableBytes);
+    return tile_bytes(kb, exact) + 1024 + kPartBytes + (exact ? 0 : kTableBytes);
   }
   // Largest reduction slice per CTA (64-blocks): keeps two CTAs per SM.
   __host__ __device__ static int kb_max(bool exact) { return NT == 1 ? 64 : (exact ? 40 : 32); }
@@ -153,11 +145,17 @@ struct FwdSmem {
 
 // EXACT = false: the unscaled-codebook table above (fp32 block scales after the
 // MMAs).  EXACT = true: each block's operand values are the reference decoder's
-// fp16(NF4[i] * scale) -- the four lanes of a quad each build a quarter of the
-// block's 16-entry table (four products rounded once) and exchange them by
-// shuffles, then every packed word is expanded through the table with byte
-// permutes (nf4_expand8, as in the tcgen05 kernels); the MMAs then accumulate
-// the decoded weights directly.  The exact mode has no reduction-length limit.
+// fp16(NF4[i] * scale), and the k order inside the MMAs is permuted so that one
+// lane owns whole blocks: in a load group of four blocks, lane t of a quad takes
+// block t of its two rows (all 32 packed bytes of each), builds that block's
+// 16-entry table itself (sixteen products rounded once, no exchange between
+// lanes) and expands its eight packed words through it with byte permutes
+// (nf4_expand8, as in the tcgen05 kernels).  MMA step j of the group multiplies,
+// in lane t's k slots {2t, 2t+1, 2t+8, 2t+9}, elements 4j .. 4j+3 of block t; the
+// activation fragment of the same lane reads those elements of its token row, so
+// the permutation costs nothing (each lane reads its block's 128 activation bytes
+// as eight 16-byte loads).  The MMAs accumulate the decoded weights directly; the
+// exact mode has no reduction-length limit.
 template <int NT, bool EXACT>
 __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -166,6 +164,8 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   // columns, two for 16 (their fragments need the registers).
   constexpr int kSlots = NT == 1 ? 3 : 2;
   constexpr int kAhead = kSlots - 1;
+  // Bytes of one 64-block in a token row of the activation tile.
+  constexpr uint32_t kXBlock = EXACT ? S::kExactBlockBytes : 128;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lane4 = static_cast<uint32_t>(lane) << 2;
@@ -175,10 +175,10 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   int64_t kb1 = kb0 + a.kb_split;
   if (kb1 > kblocks) kb1 = kblocks;
   const int kb_cta = kb1 > kb0 ? static_cast<int>(kb1 - kb0) : 0;
-  const size_t pitch = S::pitch(a.kb_split);
+  const size_t pitch = S::pitch(a.kb_split, EXACT);
   uint8_t* xs = dsm;
   float* red = reinterpret_cast<float*>(dsm);  // reused once every warp is past the tile
-  float* code2_s = reinterpret_cast<float*>(dsm + S::tile_bytes(a.kb_split));
+  float* code2_s = reinterpret_cast<float*>(dsm + S::tile_bytes(a.kb_split, EXACT));
   float* part = code2_s + 256;
   uint32_t* table = reinterpret_cast<uint32_t*>(part + kWarps * 256);  // lookup mode only
 
@@ -189,7 +189,9 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
       const int tok = i / chunks, c = i % chunks;
       const bool ok = tok < a.M;
       const __half* src = ok ? a.x + tok * a.K + kb0 * 64 + c * 8 : a.x;
-      lora::cp_async16(smem_addr(xs + tok * pitch + c * 16), src, ok);
+      const uint32_t dst = static_cast<uint32_t>(tok * pitch) + static_cast<uint32_t>(c >> 3) * kXBlock +
+                           static_cast<uint32_t>(c & 7) * 16;
+      lora::cp_async16(smem_addr(xs + dst), src, ok);
     }
     lora::cp_async_commit();
   }
@@ -209,25 +211,38 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   const int nb = rb1 > rb0 ? rb1 - rb0 : 0;
   const int64_t row_bytes = a.K / 2;
   // Byte and block offsets of the weight fit 32 bits (checked by the host).
-  const uint8_t* p_g = a.packed + static_cast<uint32_t>((ok_g ? n_g : 0) * row_bytes + (kb0 + rb0) * 32 + 8 * t);
-  const uint8_t* p_g8 = a.packed + static_cast<uint32_t>((ok_g8 ? n_g8 : 0) * row_bytes + (kb0 + rb0) * 32 + 8 * t);
+  // Lane t's piece of each block: bytes 8t .. 8t + 7 (lookup mode), or the whole
+  // of block t of each group (exact mode).
+  const uint32_t lane_off = EXACT ? 32u * t : 8u * t;
+  const uint8_t* p_g = a.packed + static_cast<uint32_t>((ok_g ? n_g : 0) * row_bytes + (kb0 + rb0) * 32 + lane_off);
+  const uint8_t* p_g8 = a.packed + static_cast<uint32_t>((ok_g8 ? n_g8 : 0) * row_bytes + (kb0 + rb0) * 32 + lane_off);
   const uint32_t q_g = static_cast<uint32_t>((ok_g ? n_g : 0) * kblocks + kb0 + rb0);
   const uint32_t q_g8 = static_cast<uint32_t>((ok_g8 ? n_g8 : 0) * kblocks + kb0 + rb0);
   const int ng = nb / kGroup;  // runs are whole groups of four blocks
 
-  // Register ring of kSlots groups: per group the two rows' 8-byte pieces of four
-  // blocks, the four absmax bytes of each row (one 32-bit word: groups start on a
-  // multiple of four blocks) and the row's absmax2 (the same for the four blocks).
+  // Register ring of kSlots groups: per group the two rows' packed bytes (lookup
+  // mode: an 8-byte piece of each of the four blocks; exact mode: all 32 bytes of
+  // block t), the four absmax bytes of each row (one 32-bit word: groups start on
+  // a multiple of four blocks) and the row's absmax2 (the same for the four blocks).
   uint2 pk[kSlots][kGroup][2];
+  uint4 pe[kSlots][2][2];
   uint32_t qw[kSlots][2];
   float a2[kSlots][2];
   auto load = [&](int gi, int slot) {
     if (gi < ng) {
       const uint32_t boff = static_cast<uint32_t>(gi) * (kGroup * 32);
+      if constexpr (EXACT) {
 #pragma unroll
-      for (int b = 0; b < kGroup; ++b) {
-        pk[slot][b][0] = __ldcs(reinterpret_cast<const uint2*>(p_g + boff + b * 32));
-        pk[slot][b][1] = __ldcs(reinterpret_cast<const uint2*>(p_g8 + boff + b * 32));
+        for (int h = 0; h < 2; ++h) {
+          pe[slot][0][h] = __ldcs(reinterpret_cast<const uint4*>(p_g + boff + h * 16));
+          pe[slot][1][h] = __ldcs(reinterpret_cast<const uint4*>(p_g8 + boff + h * 16));
+        }
+      } else {
+#pragma unroll
+        for (int b = 0; b < kGroup; ++b) {
+          pk[slot][b][0] = __ldcs(reinterpret_cast<const uint2*>(p_g + boff + b * 32));
+          pk[slot][b][1] = __ldcs(reinterpret_cast<const uint2*>(p_g8 + boff + b * 32));
+        }
       }
       const uint32_t qo = static_cast<uint32_t>(gi) * kGroup;
       qw[slot][0] = __ldg(reinterpret_cast<const uint32_t*>(a.qabs + q_g + qo));
@@ -247,16 +262,16 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   __syncthreads();  // table, code2 and activation tile ready
 
   // Activation rows of this lane's B fragments (token g + 8 nt).
+  // Lookup mode: lane t's 16-element piece of each block; exact mode: block t of
+  // each group.
   uint32_t xrow[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    xrow[nt] = smem_addr(xs) + static_cast<uint32_t>((g + 8 * nt) * pitch) + static_cast<uint32_t>(rb0) * 128 + 32 * t;
+    xrow[nt] = smem_addr(xs) + static_cast<uint32_t>((g + 8 * nt) * pitch) + static_cast<uint32_t>(rb0) * kXBlock +
+               (EXACT ? kXBlock * t : 32u * t);
   }
   const float soff = off;
   const uint32_t tb = smem_addr(table) + lane4;
-  float nf4q[4];  // code values 4t .. 4t + 3 (the quarter of a block table this lane builds)
-#pragma unroll
-  for (int i = 0; i < 4; ++i) nf4q[i] = c_nf4_values[4 * t + i];
   const uint32_t c2s = smem_addr(code2_s);
 
   for (int G = 0; G < ng; G += kSlots) {
@@ -265,6 +280,36 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
       const int gi = G + sl;
       if (gi < ng) {
         load(gi + kAhead, (sl + kAhead) % kSlots);
+        if constexpr (EXACT) {
+          // Block t of the group, rows g and g + 8: own tables, eight words each.
+          const uint32_t sh = 8u * t;
+          const float sc_g = ok_g ? __fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][0] >> sh) & 0xFFu) * 4), a2[sl][0]), soff) : 0.0f;
+          const float sc_g8 = ok_g8 ? __fadd_rn(__fmul_rn(lds_f32(c2s + ((qw[sl][1] >> sh) & 0xFFu) * 4), a2[sl][1]), soff) : 0.0f;
+          uint32_t Lg[4], Hg[4], L8[4], H8[4];
+          gemm::nf4_table(sc_g, Lg, Hg);
+          gemm::nf4_table(sc_g8, L8, H8);
+          const uint32_t wg[8] = {pe[sl][0][0].x, pe[sl][0][0].y, pe[sl][0][0].z, pe[sl][0][0].w,
+                                  pe[sl][0][1].x, pe[sl][0][1].y, pe[sl][0][1].z, pe[sl][0][1].w};
+          const uint32_t w8[8] = {pe[sl][1][0].x, pe[sl][1][0].y, pe[sl][1][0].z, pe[sl][1][0].w,
+                                  pe[sl][1][1].x, pe[sl][1][1].y, pe[sl][1][1].z, pe[sl][1][1].w};
+          const uint32_t xg = static_cast<uint32_t>(gi) * (kGroup * kXBlock);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 eg = gemm::nf4_expand8(wg[i], Lg, Hg);
+            const uint4 e8 = gemm::nf4_expand8(w8[i], L8, H8);
+            const uint32_t a0[4] = {eg.x, e8.x, eg.y, e8.y};  // elements 8i .. 8i + 3
+            const uint32_t a1[4] = {eg.z, e8.z, eg.w, e8.w};  // elements 8i + 4 .. 8i + 7
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              uint32_t xf[4];
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(xf[0]), "=r"(xf[1]), "=r"(xf[2]), "=r"(xf[3]) : "r"(xrow[nt] + xg + 16 * i));
+              lora::mma16816(acc[nt], a0, xf[0], xf[1]);
+              lora::mma16816(acc[nt], a1, xf[2], xf[3]);
+            }
+          }
+          continue;
+        }
 #pragma unroll
         for (int b = 0; b < kGroup; ++b) {
           const uint32_t blk = static_cast<uint32_t>(gi * kGroup + b);
@@ -281,58 +326,34 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
                          : "=r"(xf[nt][4]), "=r"(xf[nt][5]), "=r"(xf[nt][6]), "=r"(xf[nt][7]) : "r"(addr + 16));
           }
           const uint32_t wg[2] = {pk[sl][b][0].x, pk[sl][b][0].y}, wg8[2] = {pk[sl][b][1].x, pk[sl][b][1].y};
-          if constexpr (EXACT) {
-            uint32_t Lg[4], Hg[4], L8[4], H8[4];
-            quad_table(sc_g, nf4q, t, Lg, Hg);
-            quad_table(sc_g8, nf4q, t, L8, H8);
-            uint4 eg[2], e8[2];
+          const float s_g = __fmul_rn(sc_g, kInvAlpha), s_g8 = __fmul_rn(sc_g8, kInvAlpha);
+          float ct[NT][4];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              eg[h] = gemm::nf4_expand8(wg[h], Lg, Hg);
-              e8[h] = gemm::nf4_expand8(wg8[h], L8, H8);
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4& A = eg[j >> 1];
-              const uint4& B8 = e8[j >> 1];
-              uint32_t af[4];
-              af[0] = (j & 1) ? A.z : A.x;
-              af[1] = (j & 1) ? B8.z : B8.x;
-              af[2] = (j & 1) ? A.w : A.y;
-              af[3] = (j & 1) ? B8.w : B8.y;
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) lora::mma16816(acc[nt], af, xf[nt][2 * j], xf[nt][2 * j + 1]);
-            }
-          } else {
-            const float s_g = __fmul_rn(sc_g, kInvAlpha), s_g8 = __fmul_rn(sc_g8, kInvAlpha);
-            float ct[NT][4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint32_t af[4];
-              if ((j & 1) == 0) {
-                af[0] = lookup<0>(tb, wg[j >> 1]);
-                af[1] = lookup<0>(tb, wg8[j >> 1]);
-                af[2] = lookup<1>(tb, wg[j >> 1]);
-                af[3] = lookup<1>(tb, wg8[j >> 1]);
-              } else {
-                af[0] = lookup<2>(tb, wg[j >> 1]);
-                af[1] = lookup<2>(tb, wg8[j >> 1]);
-                af[2] = lookup<3>(tb, wg[j >> 1]);
-                af[3] = lookup<3>(tb, wg8[j >> 1]);
-              }
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                if (j == 0) mma16816_z(ct[nt], af, xf[nt][0], xf[nt][1]);
-                else lora::mma16816(ct[nt], af, xf[nt][2 * j], xf[nt][2 * j + 1]);
-              }
+          for (int j = 0; j < 4; ++j) {
+            uint32_t af[4];
+            if ((j & 1) == 0) {
+              af[0] = lookup<0>(tb, wg[j >> 1]);
+              af[1] = lookup<0>(tb, wg8[j >> 1]);
+              af[2] = lookup<1>(tb, wg[j >> 1]);
+              af[3] = lookup<1>(tb, wg8[j >> 1]);
+            } else {
+              af[0] = lookup<2>(tb, wg[j >> 1]);
+              af[1] = lookup<2>(tb, wg8[j >> 1]);
+              af[2] = lookup<3>(tb, wg[j >> 1]);
+              af[3] = lookup<3>(tb, wg8[j >> 1]);
             }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              acc[nt][0] = fmaf(s_g, ct[nt][0], acc[nt][0]);
-              acc[nt][1] = fmaf(s_g, ct[nt][1], acc[nt][1]);
-              acc[nt][2] = fmaf(s_g8, ct[nt][2], acc[nt][2]);
-              acc[nt][3] = fmaf(s_g8, ct[nt][3], acc[nt][3]);
+              if (j == 0) mma16816_z(ct[nt], af, xf[nt][0], xf[nt][1]);
+              else lora::mma16816(ct[nt], af, xf[nt][2 * j], xf[nt][2 * j + 1]);
             }
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] = fmaf(s_g, ct[nt][0], acc[nt][0]);
+            acc[nt][1] = fmaf(s_g, ct[nt][1], acc[nt][1]);
+            acc[nt][2] = fmaf(s_g8, ct[nt][2], acc[nt][2]);
+            acc[nt][3] = fmaf(s_g8, ct[nt][3], acc[nt][3]);
           }
         }
       }
