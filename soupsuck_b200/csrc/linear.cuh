@@ -90,10 +90,11 @@ inline int nf4_linear_fallback(bool dx, const uint16_t* act, int64_t m, const sb
   return check_launch("fallback_gemm_kernel");
 }
 
-// Small-M forward kernel choice, read per call: SB_SMALLM=mma takes the
-// decode-to-shared mma.sync kernel (nf4_smallm.cuh), "lut" the unscaled-table
-// lookup mode of nf4_lut.cuh (reductions <= 9216), "exact" its exact-decode
-// mode; unset takes the exact mode.
+// Small-M kernel choice, read per call: SB_SMALLM=mma takes the decode-to-shared
+// mma.sync kernel (nf4_smallm.cuh) for the forward and dX, "lut" the
+// unscaled-table lookup mode of nf4_lut.cuh for the forward (reductions <= 9216),
+// "exact" its exact-decode mode; unset takes the exact mode.  Except under "mma",
+// dX takes nf4_lut.cuh's warp-staged dX kernel.
 enum SmallmKernel { kSmallmExact = 0, kSmallmLut = 1, kSmallmMma = 2 };
 inline int smallm_kernel() {
   const char* e = std::getenv("SB_SMALLM");
@@ -127,6 +128,9 @@ inline int nf4_linear(bool dx, const uint16_t* act, int64_t m, const sb_nf4_weig
     const int kind = smallm_kernel();
     if (!dx && kind != kSmallmMma && lut::fwd_ok(m, w->n_out, w->k_in, kind == kSmallmExact)) {
       return lut::run_fwd(act, m, *w, bias, lora_a, lora_b, r, out, kind == kSmallmExact, st);
+    }
+    if (dx && kind != kSmallmMma && lut::dx_ok(m, w->n_out, w->k_in)) {
+      return lut::run_dx(act, m, *w, lora_a, lora_b, r, out, st);
     }
     return smallm::run(dx, act, m, *w, bias, lora_a, lora_b, r, out, workspace, workspace_bytes, st);
   }

@@ -114,6 +114,41 @@ struct FwdArgs {
   __half* y;              // [M, N]
 };
 
+// Cluster epilogue shared by the forward and dX kernels.  `part` holds this CTA's
+// partial sums [rows_cta][16] (row = output column, 16 token slots).  Rank q of
+// the cluster finishes a contiguous share of the rows, summing the partials of
+// all ranks in rank order through distributed shared memory, adds the LoRA term
+// la . lb^T and the bias and stores fp16 y[tok][n_base + row] (row stride width).
+__device__ __forceinline__ void cluster_finish(const float* part, int rows_cta, int64_t n_base, int64_t width,
+                                               int M, int splits, uint32_t rank, const __half* bias,
+                                               const __half* la, const __half* lb, int r, __half* y) {
+  gemm::pair::cluster_sync_all();
+  const uint32_t part_s = smem_addr(part);
+  const int share = (rows_cta + splits - 1) / splits;
+  const int row0 = static_cast<int>(rank) * share;
+  const int nrows = row0 < rows_cta ? (rows_cta - row0 < share ? rows_cta - row0 : share) : 0;
+  for (int e = threadIdx.x; e < nrows * M; e += blockDim.x) {
+    const int tok = e / nrows, row = row0 + e % nrows;
+    const int64_t n = n_base + row;
+    if (n >= width) continue;
+    float v = 0.0f;
+    for (int q = 0; q < splits; ++q) {
+      const uint32_t addr = gemm::pair::map_to_rank(part_s + static_cast<uint32_t>((row * 16 + tok) * 4), q);
+      float pv;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(addr) : "memory");
+      v += pv;
+    }
+    if (r > 0) {
+      float l = 0.0f;
+      for (int j = 0; j < r; ++j) l = fmaf(__half2float(la[tok * r + j]), __half2float(lb[n * r + j]), l);
+      v += l;
+    }
+    if (bias) v = __fadd_rn(v, __half2float(bias[n]));
+    y[static_cast<int64_t>(tok) * width + n] = __float2half_rn(v);
+  }
+  gemm::pair::cluster_sync_all();  // no CTA leaves while another reads its partial
+}
+
 // Dynamic shared memory of the forward kernel: activation tile, code2 table,
 // per-warp fragments, CTA partial.
 //
@@ -308,8 +343,7 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
               lora::mma16816(acc[nt], a1, xf[2], xf[3]);
             }
           }
-          continue;
-        }
+        } else {
 #pragma unroll
         for (int b = 0; b < kGroup; ++b) {
           const uint32_t blk = static_cast<uint32_t>(gi * kGroup + b);
@@ -356,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
             acc[nt][3] = fmaf(s_g8, ct[nt][3], acc[nt][3]);
           }
         }
+        }
       }
     }
   }
@@ -382,34 +417,186 @@ __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
     for (int q = 0; q < a.kw; ++q) v += red[(q * a.rw + tile) * 256 + (row & 15) * 16 + tok];
     part[e] = v;
   }
-  // Cluster: rank q finishes its contiguous share of the CTA's rows, summing the
-  // partials of all ranks in rank order through distributed shared memory.
-  gemm::pair::cluster_sync_all();
-  const uint32_t part_s = smem_addr(part);
-  const int share = (rows_cta + a.splits - 1) / a.splits;
-  const int row0 = static_cast<int>(rank) * share;
-  const int nrows = row0 < rows_cta ? (rows_cta - row0 < share ? rows_cta - row0 : share) : 0;
-  const int64_t n_base = static_cast<int64_t>(blockIdx.x) * rows_cta;
-  for (int e = tid; e < nrows * a.M; e += kThreads) {
-    const int tok = e / nrows, row = row0 + e % nrows;
-    const int64_t n = n_base + row;
-    if (n >= a.N) continue;
-    float v = 0.0f;
-    for (int q = 0; q < a.splits; ++q) {
-      const uint32_t addr = gemm::pair::map_to_rank(part_s + static_cast<uint32_t>((row * 16 + tok) * 4), q);
-      float pv;
-      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(addr) : "memory");
-      v += pv;
+  cluster_finish(part, rows_cta, static_cast<int64_t>(blockIdx.x) * rows_cta, a.N, a.M, a.splits, rank, a.bias,
+                 a.la, a.lb, a.r, a.y);
+}
+
+// ------------------------------------------------------------------ dX
+// dX = dY . deq(W) at M <= 16: output column c = k_in index, reduction over the
+// weight rows n.  The decoded weight enters the MMA as its A operand transposed
+// (A[c][n] = W[n][c]), which mma.sync cannot take from registers decoded along
+// k, so each warp stages its decode in shared memory and reads it back with
+// ldmatrix.trans:
+//
+//   * a warp step covers 32 weight rows x one 64-column block; lane l decodes row
+//     n0 + 32 s + l of the block -- its 32 packed bytes from global memory, its own
+//     16-entry table fp16(NF4[i] * scale) (the reference decoder's values, one
+//     rounding), eight nf4_expand8 -- into the warp's private 32 x 64 fp16 tile
+//     (4 KB, 16-byte chunks XOR-swizzled by row: conflict-free stores and
+//     ldmatrix), then __syncwarp;
+//   * the warp multiplies the tile as 2 (rows) x 4 (column groups) m16n8k16 MMAs
+//     per 8 tokens: A from ldmatrix.x4.trans, B = dY^T fragments (two halves of a
+//     dY row at adjacent weight rows) loaded straight from global memory (L2),
+//     two steps ahead with the packed bytes;
+//   * a CTA is one column block x 8 warps on consecutive row runs; the warps'
+//     partials add in warp order in shared memory, a cluster of S CTAs along
+//     grid.y splits the rows further and cluster_finish adds the ranks in order,
+//     then the LoRA term, and stores fp16.  One launch, no workspace, deterministic.
+struct DxArgs {
+  const __half* dy;       // [M, N] row-major
+  int M;
+  int64_t N, K;           // reduction length (n_out), output columns (k_in)
+  const uint8_t* packed;
+  const uint8_t* qabs;
+  const float* absmax2;
+  const float* code2;
+  const float* offset;
+  int rows_warp;          // weight rows per warp (multiple of 32); a CTA covers 8 runs
+  int splits;             // cluster size along grid.y
+  const __half* la;       // [M, r] (LoRA: y += la . lb^T) or null
+  const __half* lb;       // [K, r]
+  int r;
+  __half* y;              // [M, K]
+};
+
+constexpr int kDxRows = 32;                     // weight rows per warp step (one per lane)
+constexpr int kDxTile = kDxRows * 128;          // decoded tile per warp: 32 rows x 64 fp16
+constexpr int kDxSmem = kWarps * kDxTile + 1024 + 64 * 16 * 4;  // tiles | code2 | CTA partial
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 2) lut_dx_kernel(const DxArgs a) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  // Three ring slots (two steps in flight) for 8 tokens, two for 16.
+  constexpr int kSlots = NT == 1 ? 3 : 2, kAhead = kSlots - 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t rank = gemm::pair::cluster_rank();
+  const int64_t cb = blockIdx.x;
+  const int64_t kblocks = a.K / 64, row_bytes = a.K / 2;
+  const uint32_t tile = smem_addr(dsm + warp * kDxTile);
+  float* red = reinterpret_cast<float*>(dsm);  // [warp][64 columns][16 tokens] once the tiles are dead
+  float* code2_s = reinterpret_cast<float*>(dsm + kWarps * kDxTile);
+  float* part = code2_s + 256;                 // [64 columns][16 tokens]
+  for (int i = tid; i < 256; i += kThreads) code2_s[i] = __ldg(a.code2 + i);
+  const float off = __ldg(a.offset);
+
+  // This warp's rows [n0, n1); n1 is even (N % 8 == 0, runs are multiples of 32).
+  const int64_t n0 = (static_cast<int64_t>(rank) * kWarps + warp) * a.rows_warp;
+  int64_t n1 = n0 + a.rows_warp;
+  if (n1 > a.N) n1 = a.N;
+  const int steps = n1 > n0 ? static_cast<int>((n1 - n0 + kDxRows - 1) / kDxRows) : 0;
+
+  // Register ring: the lane's 32 packed bytes, absmax byte and absmax2 of its row,
+  // and the dY^T fragments of the step (rows 16 ks + 2t (+8), tokens g + 8 nt).
+  uint4 pw[kSlots][2];
+  uint32_t qb[kSlots];
+  float a2[kSlots];
+  uint32_t yf[kSlots][NT][2][2];
+  auto load = [&](int s, int slot) {
+    if (s < steps) {
+      const int64_t n = n0 + static_cast<int64_t>(s) * kDxRows + lane;
+      const bool ok = n < n1;
+      // Byte and block offsets of the weight fit 32 bits (checked by the host).
+      const uint32_t po = ok ? static_cast<uint32_t>(n * row_bytes + cb * 32) : 0u;
+      const uint32_t qo = ok ? static_cast<uint32_t>(n * kblocks + cb) : 0u;
+      pw[slot][0] = __ldcs(reinterpret_cast<const uint4*>(a.packed + po));
+      pw[slot][1] = __ldcs(reinterpret_cast<const uint4*>(a.packed + po + 16));
+      qb[slot] = __ldg(a.qabs + qo);
+      a2[slot] = __ldg(a.absmax2 + (qo >> 8));
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int tok = g + 8 * nt;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int64_t nn = n0 + static_cast<int64_t>(s) * kDxRows + 16 * ks + 2 * t + 8 * h;
+            yf[slot][nt][ks][h] = (tok < a.M && nn < n1)
+                                      ? __ldg(reinterpret_cast<const uint32_t*>(a.dy + tok * a.N + nn))
+                                      : 0u;
+          }
+        }
+      }
     }
-    if (a.r > 0) {
-      float l = 0.0f;
-      for (int j = 0; j < a.r; ++j) l = fmaf(__half2float(a.la[tok * a.r + j]), __half2float(a.lb[n * a.r + j]), l);
-      v += l;
+  };
+#pragma unroll
+  for (int q = 0; q < kAhead; ++q) load(q, q);
+
+  float acc[4][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
+  __syncthreads();  // code2 table ready
+
+  const uint32_t c2s = smem_addr(code2_s);
+  const uint32_t my_row = tile + static_cast<uint32_t>(lane) * 128;
+  const uint32_t swz = static_cast<uint32_t>(lane & 7);
+  // ldmatrix.x4.trans addresses: matrix j = lane / 8 holds tile rows 8 (j / 2) + 0..7
+  // and 16-byte chunk j % 2 of the 16-column group.
+  const int lm_row = (lane & 7) + 8 * ((lane >> 3) >> 1), lm_chunk = (lane >> 3) & 1;
+
+  for (int S = 0; S < steps; S += kSlots) {
+#pragma unroll
+    for (int sl = 0; sl < kSlots; ++sl) {
+      const int s = S + sl;
+      if (s < steps) {
+        load(s + kAhead, (sl + kAhead) % kSlots);
+        const bool ok = n0 + static_cast<int64_t>(s) * kDxRows + lane < n1;
+        const float scale = ok ? __fadd_rn(__fmul_rn(lds_f32(c2s + qb[sl] * 4), a2[sl]), off) : 0.0f;
+        uint32_t L[4], H[4];
+        gemm::nf4_table(scale, L, H);
+        const uint32_t w[8] = {pw[sl][0].x, pw[sl][0].y, pw[sl][0].z, pw[sl][0].w,
+                               pw[sl][1].x, pw[sl][1].y, pw[sl][1].z, pw[sl][1].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 e = gemm::nf4_expand8(w[i], L, H);
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};"
+                       :: "r"(my_row + ((static_cast<uint32_t>(i) ^ swz) << 4)), "r"(e.x), "r"(e.y), "r"(e.z), "r"(e.w)
+                       : "memory");
+        }
+        __syncwarp();
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const int row = 16 * ks + lm_row;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            const int chunk = 2 * mt + lm_chunk;
+            uint32_t af[4];
+            lora::ldsm_x4_trans(tile + static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4)), af);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) lora::mma16816(acc[mt][nt], af, yf[sl][nt][ks][0], yf[sl][nt][ks][1]);
+          }
+        }
+        __syncwarp();  // every lane's ldmatrix is done before the next step overwrites the tile
+      }
     }
-    if (a.bias) v = __fadd_rn(v, __half2float(a.bias[n]));
-    a.y[static_cast<int64_t>(tok) * a.N + n] = __float2half_rn(v);
   }
-  gemm::pair::cluster_sync_all();  // no CTA leaves while another reads its partial
+
+  // Warps add in warp order: D rows = columns 16 mt + g (+8), D columns = tokens 8 nt + 2t (+1).
+  __syncthreads();  // the tiles are dead: their space takes the warp partials
+  {
+    float* mine = red + warp * 1024;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int col = 16 * mt + g, tok = 8 * nt + 2 * t;
+        mine[col * 16 + tok] = acc[mt][nt][0];
+        mine[col * 16 + tok + 1] = acc[mt][nt][1];
+        mine[(col + 8) * 16 + tok] = acc[mt][nt][2];
+        mine[(col + 8) * 16 + tok + 1] = acc[mt][nt][3];
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < 64 * 16; e += kThreads) {
+    float v = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kWarps; ++q) v += red[q * 1024 + e];
+    part[e] = v;
+  }
+  cluster_finish(part, 64, cb * 64, a.K, a.M, a.splits, rank, nullptr, a.la, a.lb, a.r, a.y);
 }
 
 // ------------------------------------------------------------------ host side
@@ -523,6 +710,87 @@ inline int run_fwd(const uint16_t* act, int64_t m, const sb_nf4_weight& w, const
   a.y = reinterpret_cast<__half*>(out);
   if (exact) return pl.nt == 1 ? launch_fwd<1, true>(pl, a, st) : launch_fwd<2, true>(pl, a, st);
   return pl.nt == 1 ? launch_fwd<1, false>(pl, a, st) : launch_fwd<2, false>(pl, a, st);
+}
+
+struct DxPlan {
+  int nt, rows_warp, splits;
+  int64_t col_blocks;
+};
+
+// Work split of the dX kernel: one CTA per 64-column block and cluster rank; the
+// cluster size S fills the two CTA slots per SM (at most 8 ranks), each of the
+// 8 S warps of a column block taking an equal run of weight rows (a multiple of 32).
+inline DxPlan dx_plan(int64_t m, int64_t n, int64_t k) {
+  DxPlan p{};
+  p.nt = m <= 8 ? 1 : 2;
+  p.col_blocks = k / 64;
+  int64_t s = (2 * static_cast<int64_t>(device_sm_count())) / p.col_blocks;
+  if (s < 1) s = 1;
+  if (s > kMaxSplits) s = kMaxSplits;
+  const int64_t runs = s * kWarps;
+  const int64_t rows = ((n + runs - 1) / runs + kDxRows - 1) / kDxRows * kDxRows;
+  p.rows_warp = static_cast<int>(rows);
+  p.splits = static_cast<int>((n + kWarps * rows - 1) / (kWarps * rows));
+  return p;
+}
+
+inline bool dx_ok(int64_t m, int64_t n, int64_t k) {
+  return m >= 1 && m <= 16 && k % 64 == 0 && n % 8 == 0 && n * (k / 2) < (int64_t(1) << 32) &&
+         k / 64 < (int64_t(1) << 31);
+}
+
+template <int NT>
+inline int launch_dx(const DxPlan& pl, const DxArgs& a, cudaStream_t st) {
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(lut_dx_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDxSmem);
+      if (e != cudaSuccess) return fail(SB_ECUDA, std::string("lut dx smem attribute: ") + cudaGetErrorString(e));
+      configured[dev] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.col_blocks), static_cast<unsigned>(pl.splits), 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kDxSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(pl.splits);
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lut_dx_kernel<NT>, a);
+  if (e != cudaSuccess) return fail(SB_ECUDA, std::string("lut_dx_kernel launch: ") + cudaGetErrorString(e));
+  count_launch();
+  return check_launch("lut_dx_kernel");
+}
+
+inline int run_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight& w, const uint16_t* lora_a,
+                  const uint16_t* lora_b, int r, uint16_t* out, cudaStream_t st) {
+  const DxPlan pl = dx_plan(m, w.n_out, w.k_in);
+  DxArgs a{};
+  a.dy = reinterpret_cast<const __half*>(dy);
+  a.M = static_cast<int>(m);
+  a.N = w.n_out;
+  a.K = w.k_in;
+  a.packed = w.packed;
+  a.qabs = w.qabs;
+  a.absmax2 = w.absmax2;
+  a.code2 = w.code2;
+  a.offset = w.offset;
+  a.rows_warp = pl.rows_warp;
+  a.splits = pl.splits;
+  a.la = reinterpret_cast<const __half*>(lora_a);
+  a.lb = reinterpret_cast<const __half*>(lora_b);
+  a.r = r;
+  a.y = reinterpret_cast<__half*>(out);
+  return pl.nt == 1 ? launch_dx<1>(pl, a, st) : launch_dx<2>(pl, a, st);
 }
 
 }  // namespace lut

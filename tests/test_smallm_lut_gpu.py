@@ -1,4 +1,4 @@
-"""The small-M (M <= 16) NF4 forward kernels against the float64 product of the decoded weight.
+"""The small-M (M <= 16) NF4 forward and dX kernels against the float64 product of the decoded weight.
 
 nf4_lut.cuh in its exact mode (the default) expands every packed word through the
 block's fp16(NF4[code] * scale) table, the reference decoder's values; in its
@@ -81,6 +81,39 @@ def test_small_m_forward_lora_bias(kernel, name, m, r):
     y = nf4_linear_raw(x, packed, st, bias=bias, lora_a=za, lora_b=lb)
     exp = O.nf4_linear_forward(np_of(x), w16) + np_of(za).astype(np.float64) @ np_of(lb).astype(np.float64).T
     _gate(y, exp + np_of(bias).astype(np.float64))
+
+
+@pytest.mark.parametrize("name", ["exact", "mma"])
+@pytest.mark.parametrize("m,n,k", [(1, 18944, 3584), (1, 3584, 18944), (8, 3584, 3584), (9, 512, 3584),
+                                   (16, 1536, 8960), (2, 200, 128), (13, 48, 64), (16, 8, 4096),
+                                   (5, 104, 192)])
+def test_small_m_dx_kernels(kernel, name, m, n, k):
+    """dX = dY . deq(W): the warp-staged kernel (default) and the decode-to-shared one
+    (SB_SMALLM=mma), over one or several cluster ranks, row runs that end inside a
+    warp step (n not a multiple of 32) and 8 or 16 token columns."""
+    from soupsuck_b200.kernels import nf4_matmul
+    kernel(name)
+    packed, st, w16 = _weight(n, k, seed=m * 17 + n + k)
+    dy = torch.randn((m, n), device="cuda", dtype=torch.float16)
+    dx = nf4_matmul(dy, packed, st, transpose=True)
+    _gate(dx, O.nf4_linear_dx(np_of(dy), w16))
+    assert torch.equal(dx, nf4_matmul(dy, packed, st, transpose=True))
+
+
+@pytest.mark.parametrize("name", ["exact", "mma"])
+@pytest.mark.parametrize("m,r", [(1, 16), (12, 64), (7, 8)])
+def test_small_m_dx_lora(kernel, name, m, r):
+    from soupsuck_b200.kernels.nf4_gemm import nf4_linear_raw
+    kernel(name)
+    n, k = 1536, 3584
+    packed, st, w16 = _weight(n, k, seed=r + 50 * m)
+    torch.manual_seed(m * r)
+    dy = torch.randn((m, n), device="cuda", dtype=torch.float16)
+    u = (torch.randn((m, r), device="cuda") * 0.5).half()
+    at = (torch.randn((k, r), device="cuda") * 0.05).half()
+    dx = nf4_linear_raw(dy, packed, st, transpose=True, lora_a=u, lora_b=at)
+    exp = O.nf4_linear_dx(np_of(dy), w16) + np_of(u).astype(np.float64) @ np_of(at).astype(np.float64).T
+    _gate(dx, exp)
 
 
 def test_small_m_no_device_errors():
