@@ -22,6 +22,11 @@ cpu_baseline = the reference's path restated on the host (oracle/cpu_path.py).
 
 Multi-GPU (torchrun, NCCL): each rank runs its own micro-batch (data parallel,
 weak scaling) and the LoRA gradients are all-reduced every step.
+
+Other workloads (their own JSON line): --workload stack times configs[2] (the
+28-layer stack over 64 synthetic variable-length batches, data parallel, strong
+scaling); --workload sweep times configs[4] (Qwen2.5-7B shapes, M from 1 to
+16384, weights N-split across the ranks).
 """
 
 from __future__ import annotations
@@ -546,6 +551,202 @@ def run_sweep(args, torch):
     return 0
 
 
+# ------------------------------------------------------------------ 28-layer stack, DP
+STACK_LAYERS, STACK_BATCHES, STACK_ROWS, STACK_LEN = 28, 64, 4, (64, 512)
+STACK_BUCKET = 128
+
+
+def stack_lengths():
+    """Real token count of each of the 64 synthetic batches (4 right-padded rows of
+    seeded lengths U[64, 512], unpadded to packed T)."""
+    import numpy as np
+    rng = np.random.default_rng(2026)
+    lens = rng.integers(STACK_LEN[0], STACK_LEN[1] + 1, size=(STACK_BATCHES, STACK_ROWS))
+    return [int(x) for x in lens.sum(axis=1)]
+
+
+def stack_step(torch, layers, x, delta, g_out, g_kv, side=None):
+    """Forward + backward of the 28-layer projection stack on one packed batch.
+    Attention and the MLP activation are outside the hot path: o_proj reads q in
+    place of the attention output (same shape), down_proj reads silu(gate) * up
+    (torch elementwise).  With ``side`` (a stream) k/v run beside q, forward and
+    (autograd keeps each backward node on its forward's stream) backward."""
+    import torch.nn.functional as F
+    from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear
+    s = ALPHA / RANK_R
+
+    def proj(layer, name, inp):
+        packed, st, a, b = layer[name]
+        return nf4_lora_linear(inp, packed, st, a, b, s)
+
+    res, dlt = x, delta
+    outs, grads = [], []
+    for layer in layers:
+        s1, y1 = add_rms_norm(res, dlt, layer["gamma_in"], EPS)
+        if side is not None:
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                k, v = proj(layer, "k", y1), proj(layer, "v", y1)
+        else:
+            k, v = proj(layer, "k", y1), proj(layer, "v", y1)
+        q = proj(layer, "q", y1)
+        o = proj(layer, "o", q)
+        s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
+        gate, up = proj(layer, "gate", y2), proj(layer, "up", y2)
+        down = proj(layer, "down", F.silu(gate) * up)
+        outs += [k, v]
+        grads += [g_kv, g_kv]
+        res, dlt = s2, down
+    outs.append(res + dlt)
+    grads.append(g_out)
+    main = torch.cuda.current_stream()
+    if side is not None:
+        main.wait_stream(side)
+    torch.autograd.backward(outs, grads)
+    if side is not None:
+        main.wait_stream(side)
+
+
+def run_stack(args, torch):
+    """the full 28-layer Qwen2.5-1.5B projection stack over 64 synthetic
+    batches, data parallel.  Rank r takes batches r, r + N, ...; one step runs all of
+    them (forward + backward, LoRA gradients accumulated) and all-reduces the LoRA
+    gradients once.  Each batch's packed length is padded up to a multiple of 128
+    rows (zero rows) so that one CUDA graph per length bucket serves every batch
+    of that bucket; FLOPs count the real tokens only."""
+    import datetime
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    from soupsuck_b200 import _lib
+
+    layers = [build_layer(torch, device, seed=100 + i) for i in range(STACK_LAYERS)]
+    params = [p for layer in layers for p in lora_params(layer)]
+    lengths = stack_lengths()
+    mine = list(range(rank, STACK_BATCHES, world))
+    buckets = sorted({-(-lengths[b] // STACK_BUCKET) * STACK_BUCKET for b in mine})
+    g = torch.Generator(device=device).manual_seed(7 + rank)
+    tmax = buckets[-1]
+    base = {"x": torch.randn((tmax, HIDDEN), device=device, dtype=torch.float16, generator=g),
+            "d": torch.randn((tmax, HIDDEN), device=device, dtype=torch.float16, generator=g),
+            "go": torch.randn((tmax, HIDDEN), device=device, dtype=torch.float16, generator=g),
+            "gkv": torch.randn((tmax, KV), device=device, dtype=torch.float16, generator=g)}
+    acc = [torch.zeros_like(p) for p in params]
+    kv_stream = None if args.no_streams else torch.cuda.Stream(device)
+
+    def inputs(t):
+        x = base["x"][:t].clone().requires_grad_()
+        d = base["d"][:t].clone().requires_grad_()
+        return x, d, base["go"][:t].contiguous(), base["gkv"][:t].contiguous()
+
+    # Warm-up eagerly once per bucket (configures kernels before capture).
+    for t in buckets:
+        for p in params:
+            p.grad = None
+        stack_step(torch, layers, *inputs(t), side=kv_stream)
+    torch.cuda.synchronize()
+    graphs = {}
+    if not args.no_graph:
+        side = torch.cuda.Stream(device)
+        for t in buckets:
+            ins = inputs(t)
+            side.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(side):
+                for p in params:
+                    p.grad = None
+                stack_step(torch, layers, *ins, side=kv_stream)
+            torch.cuda.current_stream(device).wait_stream(side)
+            torch.cuda.synchronize()
+            for p in params:
+                p.grad = None
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                stack_step(torch, layers, *ins, side=kv_stream)
+            graphs[t] = (gr, [p.grad for p in params], ins)
+        torch.cuda.synchronize()
+
+    def allreduce(tensors):
+        if dist is None:
+            return
+        flat = torch.cat([x.reshape(-1) for x in tensors])
+        dist.all_reduce(flat)
+        flat.div_(world)
+        off = 0
+        for x in tensors:
+            x.copy_(flat[off:off + x.numel()].view_as(x))
+            off += x.numel()
+
+    def step():
+        for a_ in acc:
+            a_.zero_()
+        for b in mine:
+            t = -(-lengths[b] // STACK_BUCKET) * STACK_BUCKET
+            if graphs:
+                gr, gg, _ = graphs[t]
+                gr.replay()
+            else:
+                for p in params:
+                    p.grad = None
+                stack_step(torch, layers, *inputs(t), side=kv_stream)
+                gg = [p.grad for p in params]
+            torch._foreach_add_(acc, gg)
+        allreduce(acc)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    stream = torch.cuda.current_stream(device)
+    times = []
+    nsteps = max(1, min(args.steps, 3))
+    with ClockSampler(local) as clocks:
+        for _ in range(nsteps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) / 1000.0)
+    sec = statistics.median(times)
+    if dist is not None:
+        tt = torch.tensor([sec], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        sec = float(tt.item())
+    tokens = sum(lengths)
+    padded = sum(-(-x // STACK_BUCKET) * STACK_BUCKET for x in lengths)
+    flops = sum(step_flops(x) for x in lengths) * STACK_LAYERS
+    peak_burst, peak_sust, _, _ = measured_peaks()
+    err = _lib.take_device_error(device)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "NF4 dequant-GEMM TFLOP/s fwd+bwd, 28-layer Qwen2.5-1.5B stack (configs[2])",
+            "value": flops / sec / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": nsteps,
+            "ms_per_step": 1000 * sec, "tokens_per_s": tokens / sec, "higher_is_better": True,
+            "scaling": "strong", "dtype": "f16", "data": "synthetic (seeded lengths U[64,512], 4 rows x 64 batches)",
+            "pct_peak": 100 * flops / sec / 1e12 / (peak_sust * world),
+            "peak": "sustained bf16 (MEASURED_PEAKS.json)",
+            "config": {"workload": "configs[2]: 28 layers x 7 NF4+LoRA(r=16) projections + 2 add-RMSNorm, fwd+bwd",
+                       "batches": STACK_BATCHES, "tokens": tokens, "padded_rows": padded,
+                       "bucket_rows": STACK_BUCKET, "cuda_graph": bool(graphs), "graphs": len(graphs),
+                       "streams": "k/v on a side stream" if kv_stream is not None else "one stream",
+                       "parallelism": f"dp{world}"},
+            "clocks": clocks.summary(), "device_error": err}), flush=True)
+    del graphs
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -560,8 +761,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ce", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["layer", "sweep"], default="layer",
-                    help="layer: configs[1] (the headline line); sweep: configs[4] 7B shapes")
+    ap.add_argument("--workload", choices=["layer", "sweep", "stack"], default="layer",
+                    help="layer: configs[1] (the headline line); sweep: configs[4] 7B shapes; "
+                         "stack: configs[2] 28-layer stack, data parallel")
     ap.add_argument("--kernel-case", choices=["nf4_fwd", "nf4_dx", "gemm_pass", "layer", "ce"],
                     help="run a small launch of one kernel family (for ncu) instead of the bench")
     ap.add_argument("--case-n", type=int, default=INTER)
@@ -574,6 +776,8 @@ def main():
         return kernel_case(args, torch)
     if args.workload == "sweep":
         return run_sweep(args, torch)
+    if args.workload == "stack":
+        return run_stack(args, torch)
 
     if args.impl == "reference":
         return run_reference(args, torch)
