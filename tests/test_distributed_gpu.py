@@ -7,6 +7,7 @@ Tolerances are the single-GPU gates (GEMM 2e-3 abs + 2e-3 rel; CE metric 2e-3,
 gradient 1e-2 of the ideal norm).
 """
 
+import functools
 import math
 import os
 import socket
@@ -45,7 +46,7 @@ def _run(fn):
     mp.spawn(_entry, args=(fn, _free_port()), nprocs=WORLD, join=True)
 
 
-def _nsplit(rank):
+def _nsplit(rank, m=300):
     import numpy as np
 
     from oracle import oracle as O
@@ -54,7 +55,7 @@ def _nsplit(rank):
     from soupsuck_b200.quantize import quantize_nf4
 
     dev = torch.device("cuda", rank)
-    m, n, k, r, s = 300, 1536, 1536, 16, 2.0
+    n, k, r, s = 1536, 1536, 16, 2.0
     g = torch.Generator(device=dev).manual_seed(0)
     w = (torch.randn((n, k), device=dev, generator=g) * 0.02).half()
     packed, st = quantize_nf4(w)
@@ -84,8 +85,10 @@ def _nsplit(rank):
 
 
 @needs_two
-def test_nsplit_projection_matches_single_gpu():
-    _run(_nsplit)
+@pytest.mark.parametrize("m", [300, 4])
+def test_nsplit_projection_matches_single_gpu(m):
+    """m = 300 runs the tcgen05 GEMMs on each rank's shard, m = 4 the small-M kernels."""
+    _run(functools.partial(_nsplit, m=m))
 
 
 def _vocab(rank):
