@@ -94,8 +94,10 @@ int sb_nf4_linear_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight* w,
 
 /* Scratch bytes the two calls above need for these sizes, assuming 16-byte aligned
  * x/dy, packed and LoRA pointers: fp32 partial tiles and per-tile counters when the
- * tcgen05 path splits tiles across CTAs (stream-K), or the decoded weight when an
- * odd shape takes the CUDA-core path. */
+ * tcgen05 path splits tiles across CTAs (stream-K), the fp32 reduction-slice
+ * partials of the decode-to-shared small-M kernel (m <= 16 with SB_SMALLM=mma; the
+ * default small-M kernels reduce through cluster shared memory and need none), or
+ * the decoded weight when an odd shape takes the CUDA-core path. */
 size_t sb_nf4_linear_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in, int dx);
 
 /* ---------------------------------------------------------------- LoRA factors
