@@ -569,8 +569,9 @@ def stack_step(torch, layers, x, delta, g_out, g_kv, side=None):
     """Forward + backward of the 28-layer projection stack on one packed batch.
     Attention and the MLP activation are outside the hot path: o_proj reads q in
     place of the attention output (same shape), down_proj reads silu(gate) * up
-    (torch elementwise).  With ``side`` (a stream) k/v run beside q, forward and
-    (autograd keeps each backward node on its forward's stream) backward."""
+    (torch elementwise).  With ``side`` (a stream) k/v run beside q and up beside
+    gate, forward and (autograd keeps each backward node on its forward's stream)
+    backward."""
     import torch.nn.functional as F
     from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear
     s = ALPHA / RANK_R
@@ -579,27 +580,40 @@ def stack_step(torch, layers, x, delta, g_out, g_kv, side=None):
         packed, st, a, b = layer[name]
         return nf4_lora_linear(inp, packed, st, a, b, s)
 
+    main = torch.cuda.current_stream()
     res, dlt = x, delta
     outs, grads = [], []
     for layer in layers:
         s1, y1 = add_rms_norm(res, dlt, layer["gamma_in"], EPS)
         if side is not None:
-            side.wait_stream(torch.cuda.current_stream())
+            # Tensors that cross streams are recorded on the stream that reads them,
+            # so the allocator does not hand their memory to the allocating stream
+            # while the other still uses it (autograd frees them mid-backward).
+            side.wait_stream(main)
             with torch.cuda.stream(side):
                 k, v = proj(layer, "k", y1), proj(layer, "v", y1)
+            y1.record_stream(side)
         else:
             k, v = proj(layer, "k", y1), proj(layer, "v", y1)
         q = proj(layer, "q", y1)
         o = proj(layer, "o", q)
         s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
-        gate, up = proj(layer, "gate", y2), proj(layer, "up", y2)
+        if side is not None:
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                up = proj(layer, "up", y2)
+            y2.record_stream(side)
+            gate = proj(layer, "gate", y2)
+            main.wait_stream(side)
+            up.record_stream(main)
+        else:
+            gate, up = proj(layer, "gate", y2), proj(layer, "up", y2)
         down = proj(layer, "down", F.silu(gate) * up)
         outs += [k, v]
         grads += [g_kv, g_kv]
         res, dlt = s2, down
     outs.append(res + dlt)
     grads.append(g_out)
-    main = torch.cuda.current_stream()
     if side is not None:
         main.wait_stream(side)
     torch.autograd.backward(outs, grads)
@@ -737,7 +751,7 @@ def run_stack(args, torch):
             "config": {"workload": "configs[2]: 28 layers x 7 NF4+LoRA(r=16) projections + 2 add-RMSNorm, fwd+bwd",
                        "batches": STACK_BATCHES, "tokens": tokens, "padded_rows": padded,
                        "bucket_rows": STACK_BUCKET, "cuda_graph": bool(graphs), "graphs": len(graphs),
-                       "streams": "k/v on a side stream" if kv_stream is not None else "one stream",
+                       "streams": "k/v and up on a side stream" if kv_stream is not None else "one stream",
                        "parallelism": f"dp{world}"},
             "clocks": clocks.summary(), "device_error": err}), flush=True)
     del graphs
