@@ -290,9 +290,10 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
       tc_fence_before();
       mbar_arrive_cluster(leader_acc_empty + 8u * buf);
     } else if constexpr (SK) {
-      // Stream-K partial tile: park this CTA's 128 x 256 fp32 half in its slot,
-      // release TMEM, and let the last contributing pair to arrive (per half,
-      // counter tile * 2 + rank) sum all slots in pair order and run the epilogue.
+      // Stream-K partial tile: park this CTA's 128 x 256 fp32 half in its slot;
+      // the last contributing pair to arrive (per half, counter tile * 2 + rank)
+      // sums the contributions in pair order -- its own from TMEM, the others'
+      // from their slots -- and runs the epilogue.
       const int slot = uidx == 0 ? 0 : 1;
       const int cta = pair_id * 2 + static_cast<int>(rank);
       float4* mine = reinterpret_cast<float4*>(p.partials) + (static_cast<int64_t>(cta) * 2 + slot) * kSlotF4;
@@ -308,10 +309,15 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
                                             __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
         }
       }
-      tc_fence_before();
-      mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+      // The accumulator buffer stays allocated until this CTA knows whether it
+      // is the last contributor: the last one reads its own part back from TMEM
+      // instead of its slot.  Every exit releases it.
+      auto release_acc = [&]() {
+        tc_fence_before();
+        mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+      };
       __threadfence();
-      if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+      if (!epi_sync(epi_mb, epi_phase, abort_flag)) { release_acc(); break; }
       const int64_t it0 = static_cast<int64_t>(u.tile) * p.k_blocks;
       const int c_lo = sk_owner(it0, total, pairs);
       const int c_hi = sk_owner(it0 + p.k_blocks - 1, total, pairs);
@@ -320,10 +326,12 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
         const int prev = atomicAdd(counter, 1);
         *last_flag = (prev == c_hi - c_lo) ? 1 : 0;
       }
-      if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
+      if (!epi_sync(epi_mb, epi_phase, abort_flag)) { release_acc(); break; }
       const bool last = *last_flag != 0;
-      if (!epi_sync(epi_mb, epi_phase, abort_flag)) break;
-      if (last) {
+      if (!epi_sync(epi_mb, epi_phase, abort_flag)) { release_acc(); break; }
+      if (!last) {
+        release_acc();
+      } else {
         __threadfence();
         EpiState st;
         epilogue_begin<EMODE>(p, st, row, rows_valid);
@@ -333,7 +341,17 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
 #pragma unroll
           for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
           const int64_t off = static_cast<int64_t>(c * 8) * 128 + etid;
+          // Contributors in pair order (the sum does not depend on who is last);
+          // this pair's own part comes from TMEM, bit-identical to its slot.
           for (int ci = c_lo; ci <= c_hi; ++ci) {
+            if (ci == pair_id) {
+              uint32_t v[32];
+              tmem_ld32(tacc + c * 32, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sum[j] += __uint_as_float(v[j]);
+              continue;
+            }
             const int64_t first_tile = (total * ci / pairs) / p.k_blocks;
             const int cslot = first_tile == u.tile ? 0 : 1;
             const float4* src = reinterpret_cast<const float4*>(p.partials) +
@@ -352,6 +370,7 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
           for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(sum[j]);
           epilogue_chunk<EMODE>(p, st, v, row, n0 + c * 32, rows_valid);
         }
+        release_acc();
         epilogue_end<EMODE>(p, st, row, nt, rows_valid);
         if (etid == 0) *counter = 0;  // ready for the next launch
       }
