@@ -472,8 +472,10 @@ constexpr int kDxSmem = kWarps * kDxTile + 1024 + 64 * 16 * 4;  // tiles | code2
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 2) lut_dx_kernel(const DxArgs a) {
   extern __shared__ __align__(128) uint8_t dsm[];
-  // Three ring slots (two steps in flight) for 8 tokens, two for 16.
-  constexpr int kSlots = NT == 1 ? 3 : 2, kAhead = kSlots - 1;
+  // Two ring slots (the next step's loads in flight during this one): deeper
+  // rings measured slower on the 7B gate dX at M = 1 (26.9 us with 2 slots, 27.8
+  // with 3, 29.2 with 4, 28.4 with 5).
+  constexpr int kSlots = 2, kAhead = kSlots - 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t rank = gemm::pair::cluster_rank();
