@@ -195,9 +195,10 @@ template <int NT, bool EXACT>
 __global__ void __launch_bounds__(kThreads, 2) lut_fwd_kernel(const FwdArgs a) {
   extern __shared__ __align__(128) uint8_t dsm[];
   using S = FwdSmem<NT>;
-  // Register ring of load groups: three slots (two groups in flight) for 8 token
-  // columns, two for 16 (their fragments need the registers).
-  constexpr int kSlots = NT == 1 ? 3 : 2;
+  // Register ring of load groups: two slots (the next group's loads in flight
+  // during this one); three measured slower for 8 token columns (7B gate at
+  // M = 1: 20.75 against 20.35 us) and do not fit the registers of 16.
+  constexpr int kSlots = 2;
   constexpr int kAhead = kSlots - 1;
   // Bytes of one 64-block in a token row of the activation tile.
   constexpr uint32_t kXBlock = EXACT ? S::kExactBlockBytes : 128;
