@@ -828,23 +828,18 @@ def main():
             dev_in[name].grad = None
 
     def allreduce_grads(grads=None):
-        # One persistent flat fp32 buffer: gather (one cat), sum over the ranks and
-        # divide in place, scatter back with one multi-tensor copy.
         nonlocal flat_grad
         if dist is None:
             return
         grads = grads if grads is not None else [p.grad for p in params]
-        total = sum(gr.numel() for gr in grads)
-        if flat_grad is None or flat_grad.numel() != total:
-            flat_grad = torch.empty(total, device=device, dtype=grads[0].dtype)
-        torch.cat([gr.reshape(-1) for gr in grads], out=flat_grad)
-        dist.all_reduce(flat_grad)
-        flat_grad.div_(world)
-        views, off = [], 0
+        flat = torch.cat([gr.reshape(-1) for gr in grads])
+        dist.all_reduce(flat)
+        flat.div_(world)
+        off = 0
         for gr in grads:
-            views.append(flat_grad[off:off + gr.numel()].view_as(gr))
-            off += gr.numel()
-        torch._foreach_copy_(grads, views)
+            n = gr.numel()
+            gr.copy_(flat[off:off + n].view_as(gr))
+            off += n
 
     streams = None if args.no_streams else (torch.cuda.Stream(device), torch.cuda.Stream(device))
 
