@@ -253,24 +253,37 @@ def ce_forward(hidden, weight, targets, ignore_index: int = -100, chunk: int = 4
     return loss.astype(F32), entropy.astype(F32), best.astype(np.int64), lse.astype(F32)
 
 
-def ce_backward_ideal(hidden, weight, targets, grad, ignore_index: int = -100):
+def ce_backward_ideal(hidden, weight, targets, grad, ignore_index: int = -100,
+                      chunk: int = 8192):
     """Analytic dX of CE at the fp16-rounded logits: (softmax - onehot)*g @ W16.
 
     This is the 'ideal' gradient of solution/tests/test_cross_entropy.py:89-98
-    that the reference's own tests bound its result against.
+    that the reference's own tests bound its result against.  Two passes over
+    vocabulary chunks (exact float64 log-sum-exp, then the weighted sum), so a
+    full 151,936-row head never has to be widened to float64 at once.
     """
     targets = np.asarray(targets, dtype=np.int64)
-    z = fp16_logits(hidden, weight).astype(F64)
-    z = z - z.max(1, keepdims=True)
-    p = np.exp(z)
-    p /= p.sum(1, keepdims=True)
+    weight = np.asarray(weight)
+    n, v = targets.shape[0], weight.shape[0]
+    m = np.full(n, -np.inf)
+    s = np.zeros(n)
+    for start in range(0, v, chunk):
+        z = fp16_logits(hidden, weight[start:start + chunk]).astype(F64)
+        new_m = np.maximum(m, z.max(1))
+        s = s * np.exp(m - new_m) + np.exp(z - new_m[:, None]).sum(1)
+        m = new_m
+    lse = m + np.log(s)
     valid = targets != ignore_index
-    rows = np.arange(targets.shape[0])
-    p[rows[valid], targets[valid]] -= 1.0
-    p[~valid] = 0.0
-    p *= np.asarray(grad, dtype=F64)[:, None]
-    p[~valid] = 0.0
-    return p @ np.asarray(weight).astype(F16).astype(F64)
+    g = np.where(valid, np.asarray(grad, dtype=F64), 0.0)
+    rows = np.arange(n)
+    out = np.zeros((n, weight.shape[1]), dtype=F64)
+    for start in range(0, v, chunk):
+        wc = weight[start:start + chunk].astype(F16).astype(F64)
+        p = np.exp(fp16_logits(hidden, weight[start:start + chunk]).astype(F64) - lse[:, None])
+        inside = valid & (targets >= start) & (targets < start + wc.shape[0])
+        p[rows[inside], targets[inside] - start] -= 1.0
+        out += (p * g[:, None]) @ wc
+    return out
 
 
 def ce_backward_reference(hidden, weight, targets, lse, grad, ignore_index: int = -100,
