@@ -78,17 +78,15 @@ def pass_bytes(m):
     return total
 
 
-TRAFFIC_PROFILE = ROOT / "profiles" / "nf4_gemm_pass_t3300_traffic.md"
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one 14-launch GEMM
+# pass at T=3300, from a separate ncu capture of `bench.py --kernel-case
+# gemm_pass` (ncu cannot run inside the timed bench).  A static figure: it is
+# reported as such and describes the kernels of the capture it came from.
+PASS_TRAFFIC_NCU = {3300: 536506624}
 
 
-def measured_pass_traffic(m):
-    """DRAM bytes of one GEMM pass from the committed ncu capture (T=3300 only)."""
-    if m != T_TOKENS or not TRAFFIC_PROFILE.exists():
-        return None
-    for line in TRAFFIC_PROFILE.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_pass:"):
-            return int(line.split(":")[1])
-    return None
+def static_pass_traffic(m):
+    return PASS_TRAFFIC_NCU.get(m)
 
 
 def measured_peaks():
@@ -259,29 +257,36 @@ def lora_params(layer):
 
 
 # ------------------------------------------------------------------ CPU reference
-def run_cpu_sample(torch, layer, budget_s):
-    from oracle.cpu_path import CpuProjection, threads, time_projections
-    projs = [CpuProjection(layer[name][0], layer[name][1], layer[name][2], layer[name][3],
-                           ALPHA / RANK_R) for name, _, _ in PROJ]
-    rows = 128
-    sec, flops = time_projections(projs, rows, budget_s=budget_s)
+def _cpu_projections(layer):
+    from oracle.cpu_path import CpuProjection
+    return [CpuProjection(layer[name][0], layer[name][1], layer[name][2], layer[name][3],
+                          ALPHA / RANK_R) for name, _, _ in PROJ]
+
+
+def run_cpu_sample(torch, layer, budget_s, rows=T_TOKENS):
+    """cpu_baseline: the reference path restated on the host, on the same
+    configs[1] rows as the GPU step (every pass dequantizes each weight twice)."""
+    from oracle.cpu_path import threads, time_projections
+    sec, flops = time_projections(_cpu_projections(layer), rows, budget_s=budget_s)
     return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": threads(), "kind": "port",
-            "sample": f"fwd+dX of the 7 projections on {rows} of {T_TOKENS} rows per pass "
-                      f"(dequant via C oracle on {threads()} threads + torch fp32 matmul), "
+            "same_config": rows == T_TOKENS,
+            "sample": f"fwd+dX of the 7 projections on all {rows} rows of configs[1] per pass "
+                      f"(dequant via the C oracle on {threads()} threads + torch fp32 matmul), "
                       f"{sec:.3f} s per pass"}
 
 
 def run_reference(args, torch):
-    """--impl reference: the reference's CPU path (oracle port), rank 0 only."""
+    """--impl reference: the reference's path restated on the host cores (the
+    oracle port; the reference itself is Triton for sm_75 behind bitsandbytes),
+    on the same configs[1] workload as the GPU arm; rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     layer = build_layer(torch, "cpu", seed=0)
-    from oracle.cpu_path import CpuProjection, threads, time_projections
-    projs = [CpuProjection(layer[name][0], layer[name][1], layer[name][2], layer[name][3],
-                           ALPHA / RANK_R) for name, _, _ in PROJ]
-    rows = 128
-    time_projections(projs, rows, budget_s=0.0, min_reps=max(1, min(args.warmup, 1)))
+    from oracle.cpu_path import threads, time_projections
+    projs = _cpu_projections(layer)
+    rows = args.tokens
+    time_projections(projs, rows, budget_s=0.0, min_reps=1)
     per = []
     flops = None
     for _ in range(args.steps):
@@ -293,10 +298,11 @@ def run_reference(args, torch):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000 * total / len(per), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"configs[1] sample: 7 NF4+LoRA projections fwd+dX, {rows} of "
-                                   f"{T_TOKENS} rows per step", "tokens": rows},
+            "config": {"workload": f"configs[1]: 7 NF4+LoRA(r=16) projections fwd+dX on {rows} rows "
+                                   f"(the GEMM work of the GPU arm's layer step)", "tokens": rows,
+                       "same_config": rows == T_TOKENS},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads(), "kind": "port",
-                             "sample": f"{rows} rows x 7 projections fwd+dX per step"},
+                             "sample": f"all {rows} rows x 7 projections fwd+dX per step"},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -819,7 +825,6 @@ def main():
         dev_in[name] = torch.randn(shp, device=device, dtype=torch.float16, generator=g)
     for name in ("residual", "attn", "act", "mlp_prev"):
         dev_in[name].requires_grad_()
-    flat_grad = None
 
     def zero_grads():
         for p in params:
@@ -827,19 +832,17 @@ def main():
         for name in ("residual", "attn", "act", "mlp_prev"):
             dev_in[name].grad = None
 
-    def allreduce_grads(grads=None):
-        nonlocal flat_grad
+    def allreduce_grads():
+        """Average the LoRA gradients over the ranks: one flat fp32 buffer (one
+        concatenation launch), one NCCL all-reduce, one scale.  Inside a captured
+        step this is part of the graph, so it runs right behind the backward with
+        no host round trip.  Returns the averaged flat buffer (None on one GPU)."""
         if dist is None:
-            return
-        grads = grads if grads is not None else [p.grad for p in params]
-        flat = torch.cat([gr.reshape(-1) for gr in grads])
+            return None
+        flat = torch.cat([p.grad.reshape(-1) for p in params])
         dist.all_reduce(flat)
-        flat.div_(world)
-        off = 0
-        for gr in grads:
-            n = gr.numel()
-            gr.copy_(flat[off:off + n].view_as(gr))
-            off += n
+        flat.mul_(1.0 / world)
+        return flat
 
     streams = None if args.no_streams else (torch.cuda.Stream(device), torch.cuda.Stream(device))
 
@@ -880,9 +883,10 @@ def main():
             before = _lib.launch_count()
             with torch.cuda.graph(g_):
                 layer_step(torch, layer, inputs, streams)
+                flat = allreduce_grads()
             launches_per_step = _lib.launch_count() - before
             graphs.append(g_)
-            graph_grads.append([p.grad for p in params])
+            graph_grads.append(flat if flat is not None else [p.grad for p in params])
             graph_out.append(inputs["residual"].grad)
         for g_ in graphs:
             for _ in range(2):
@@ -891,11 +895,10 @@ def main():
     graph = graphs[0] if graphs else None
 
     def run_step():
-        # With a graph the LoRA gradients live in the graph's pool and are
-        # overwritten by every replay; the all-reduce stays outside the graph.
+        # With a graph the LoRA gradients (and, on N GPUs, their all-reduced
+        # average) live in the graph's pool and are overwritten by every replay.
         if graph is not None:
             graph.replay()
-            allreduce_grads(graph_grads[0])
         else:
             device_step()
 
@@ -971,7 +974,6 @@ def main():
             copied.record(copy_stream)
             stream.wait_event(copied)
             graphs[j].replay()
-            allreduce_grads(graph_grads[j])
             out_host[j].copy_(graph_out[j], non_blocking=True)
             done[j] = torch.cuda.Event()
             done[j].record(stream)
@@ -997,6 +999,12 @@ def main():
         e2e_sec = float(tt.item())
     e2e_value = flops / e2e_sec / 1e12
 
+    # The captured steps hold NCCL work: release them before the process group.
+    torch.cuda.synchronize()
+    used_graph = graph is not None
+    graph = None
+    graphs.clear()
+    graph_grads.clear()
     if rank != 0:
         if dist is not None:
             dist.barrier()
@@ -1019,17 +1027,18 @@ def main():
                    "tokens_per_gpu": t, "global_tokens": t * world,
                    "parallelism": f"dp{world}" + (" + LoRA-grad NCCL all-reduce" if world > 1 else ""),
                    "l2": "flushed (256 MiB write) before every timed step, outside the events",
-                   "cuda_graph": graph is not None,
+                   "cuda_graph": used_graph,
                    "streams": "o/down, k/v and up on two side streams" if streams else "one stream"},
         "pct_peak": 100.0 * value / (peak_burst * world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": 1000 * e2e_sec,
                 "pipelining": "next step's host->device copy overlaps the current step (two input sets)"
-                              if graph is not None else "none"},
+                              if used_graph else "none"},
         "gpu_launches": int(launches_per_step) * args.steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_burst, "unit": "TFLOP/s",
-                     "frac": achieved / peak_burst, "traffic": measured_pass_traffic(t),
-                     "traffic_unit": "DRAM bytes per pass of the 14 launches (ncu, profiles/nf4_gemm_pass_t3300_traffic.md)",
+                     "frac": achieved / peak_burst, "traffic": static_pass_traffic(t),
+                     "traffic_source": "static ncu figure (DRAM bytes per pass of the 14 launches, "
+                                       "captured separately from this run)",
                      "algorithmic_bytes": pass_bytes(t),
                      "kernel": "pair_kernel<NF4> (cta_group::2) fwd+dX, LoRA fused",
                      "peak_source": f"{peak_kind} bf16 dense burst (MEASURED_PEAKS.json)",

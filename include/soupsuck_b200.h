@@ -215,6 +215,57 @@ size_t sb_ce_backward_workspace_bytes(int64_t t, int64_t h, int64_t v);
 int sb_ce_check_targets(const int64_t* targets, int64_t t, int64_t v, int64_t ignore_index,
                         int64_t* bad, void* stream);
 
+/* ---------------------------------------------------------------- Rotary embedding
+ * rope_pair_forward_kernel / rope_pair_backward_kernel (solution/kernels/rope.py:24-105,
+ * installed as Qwen2's apply_rotary_pos_emb by solution/rope.py:55-80): q [B, Hq, S, D]
+ * and k [B, Hk, S, D] with element strides {batch, head, token, column} (any layout),
+ * cos / sin [cs_batches (1 or B), S, D] with strides {batch, token, column = 1}.
+ * Forward (backward = 0): q_out = q*cos + rotate_half(q)*sin, every product rounded to
+ * q_out's dtype before the sum (eager PyTorch rounding; q_out_dtype = promote(q, cos)).
+ * Backward: q / k are the output gradients and q_out / k_out receive the input
+ * gradients (products rounded to their dtype).  Outputs are contiguous; a side with
+ * zero heads is skipped (its pointers may be NULL).  Bit-exact. */
+int sb_rope(const void* q, int q_dtype, const int64_t* q_strides, int64_t q_heads, void* q_out,
+            int q_out_dtype, const void* k, int k_dtype, const int64_t* k_strides, int64_t k_heads,
+            void* k_out, int k_out_dtype, const void* cos, const void* sin, int cs_dtype,
+            const int64_t* cos_strides, const int64_t* sin_strides, int64_t cs_batches,
+            int64_t batches, int64_t tokens, int64_t dim, int backward, void* stream);
+
+/* ---------------------------------------------------------------- SwiGLU (element-wise)
+ * swiglu_tile_engine (solution/kernels/swiglu_fused.py:21-78) on fp16 matrices
+ * [rows, width] with row pitches ld_* (elements): act = g * sigmoid(g) * u, and
+ * dgate = (da*u) * (p + g p (1 - p)), dup = da * g p with p = sigmoid(g), fp32 math. */
+int sb_swiglu_fwd(const uint16_t* gate, int64_t ld_gate, const uint16_t* up, int64_t ld_up, uint16_t* act,
+                  int64_t ld_act, int64_t rows, int64_t width, void* stream);
+int sb_swiglu_bwd(const uint16_t* gate, int64_t ld_gate, const uint16_t* up, int64_t ld_up,
+                  const uint16_t* grad, int64_t ld_grad, uint16_t* dgate, int64_t ld_dgate, uint16_t* dup,
+                  int64_t ld_dup, int64_t rows, int64_t width, void* stream);
+
+/* ---------------------------------------------------------------- Qwen2 MLP, fused
+ * The frozen MLP of solution/mlp.py:500-593 (gate/up projections, SwiGLU, down
+ * projection, and its backward) on NF4 weights, with the SwiGLU passes inside the
+ * GEMM epilogues.  All fp16, 16-byte aligned; N = intermediate size.
+ *
+ * sb_nf4_mlp_gate_up_fwd: gate and up [N, K] (same shape, N % 128 == 0) in ONE launch:
+ *   gate_up[m, 2N] = [X.deq(Wg)^T | X.deq(Wu)^T] (+ lora_a[m, r] . lora_b[2N, r]^T),
+ *   act[m, N] = SwiGLU(gate, up) of the fp16-rounded gate/up.  For two adapters of
+ *   rank r0, lora_a = [s X.Ag^T | s X.Au^T] and lora_b = [[Bg, 0]; [0, Bu]] (r = 2 r0).
+ * sb_nf4_mlp_down_dx: down [K_h, N]; dact = dY[m, K_h] . deq(Wd) (+ LoRA as in
+ *   sb_nf4_linear_dx) rounded to fp16, then dgate_up[m, 2N] = [dgate | dup] against
+ *   gate_up[m, 2N] (N % 64 == 0).
+ * sb_nf4_linear_dx2: the input gradient of two projections of one input, as one
+ *   reduction: dX[m, K] = dY2[m, 2N] . [deq(W1); deq(W2)] (+ lora_a[m, r] . lora_b[K, r]^T),
+ *   W1, W2 [N, K] (N % 64 == 0); workspace: sb_nf4_linear_dx2_workspace_bytes(m, N, K). */
+int sb_nf4_mlp_gate_up_fwd(const uint16_t* x, int64_t m, const sb_nf4_weight* gate, const sb_nf4_weight* up,
+                           const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* gate_up,
+                           uint16_t* act, void* stream);
+int sb_nf4_mlp_down_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight* down, const uint16_t* lora_a,
+                       const uint16_t* lora_b, int r, const uint16_t* gate_up, uint16_t* dgate_up, void* stream);
+size_t sb_nf4_linear_dx2_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in);
+int sb_nf4_linear_dx2(const uint16_t* dy2, int64_t m, const sb_nf4_weight* w1, const sb_nf4_weight* w2,
+                      const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* dx, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

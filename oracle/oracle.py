@@ -368,3 +368,70 @@ def gemm_gate(actual, expected, rtol=2e-3, atol=2e-3, rel_l2=1e-3):
     denom = float(np.linalg.norm(e)) or 1.0
     rel = float(np.linalg.norm(a - e)) / denom
     return finite and close and rel <= rel_l2, float(err.max(initial=0.0)), rel
+
+
+# --------------------------------------------------------------------------
+# Joint q/k rotary embedding (solution/kernels/rope.py:24-105)
+# --------------------------------------------------------------------------
+
+def _rope_rows(x, cos, sin, out_dtype, backward):
+    """x [B, H, S, D] (any float dtype), cos/sin [1|B, S, D]; products rounded to
+    out_dtype before the sum, the sum rounded on store (rope.py:55-58, :91-93)."""
+    x = np.asarray(x).astype(F32)
+    half = x.shape[-1] // 2
+    c = np.asarray(cos).astype(F32)[:, None]
+    s = np.asarray(sin).astype(F32)[:, None]
+    c1, c2, s1, s2 = c[..., :half], c[..., half:], s[..., :half], s[..., half:]
+    x1, x2 = x[..., :half], x[..., half:]
+    r = lambda v: v.astype(F32).astype(out_dtype).astype(F32)
+    if not backward:
+        lo = r(x1 * c1) + r((-x2) * s1)
+        hi = r(x2 * c2) + r(x1 * s2)
+    else:
+        lo = r(x1 * c1) + r(x2 * s2)
+        hi = r(x2 * c2) - r(x1 * s1)
+    return np.concatenate([lo.astype(F32), hi.astype(F32)], axis=-1).astype(out_dtype)
+
+
+def rope_forward(q, k, cos, sin):
+    """(yq, yk): y = x*cos + rotate_half(x)*sin in promote(x, cos), eager rounding."""
+    cdt = np.asarray(cos).dtype
+    return (_rope_rows(q, cos, sin, np.promote_types(np.asarray(q).dtype, cdt), False),
+            _rope_rows(k, cos, sin, np.promote_types(np.asarray(k).dtype, cdt), False))
+
+
+def rope_backward(gq, gk, cos, sin, q_dtype, k_dtype):
+    """(dq, dk): dx1 = g1*c1 + g2*s2, dx2 = g2*c2 - g1*s1, products rounded to x's dtype."""
+    return (_rope_rows(gq, cos, sin, q_dtype, True), _rope_rows(gk, cos, sin, k_dtype, True))
+
+
+# --------------------------------------------------------------------------
+# SwiGLU tile engine (solution/kernels/swiglu_fused.py:21-46)
+# --------------------------------------------------------------------------
+
+def _sigmoid32(g):
+    return (F32(1.0) / (F32(1.0) + np.exp(-g).astype(F32))).astype(F32)
+
+
+def swiglu_forward(gate, up, out_dtype=None):
+    """a = g * sigmoid(g) * u in fp32, stored in gate's dtype (swiglu_fused.py:29-46)."""
+    gate = np.asarray(gate)
+    g = gate.astype(F32)
+    u = np.asarray(up).astype(F32)
+    p = _sigmoid32(g)
+    return ((g * p).astype(F32) * u).astype(F32).astype(out_dtype or gate.dtype)
+
+
+def swiglu_backward(gate, up, grad, gate_dtype=None, up_dtype=None):
+    """dg = (da*u) * (p + a*(1-p)), du = da * a with p = sigmoid(g), a = g*p (:35-41)."""
+    gate = np.asarray(gate)
+    up = np.asarray(up)
+    g = gate.astype(F32)
+    u = up.astype(F32)
+    da = np.asarray(grad).astype(F32)
+    p = _sigmoid32(g)
+    act = (g * p).astype(F32)
+    slope = (p + (act * (F32(1.0) - p)).astype(F32)).astype(F32)
+    dg = ((da * u).astype(F32) * slope).astype(F32)
+    du = (da * act).astype(F32)
+    return dg.astype(gate_dtype or gate.dtype), du.astype(up_dtype or up.dtype)

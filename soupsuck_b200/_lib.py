@@ -23,6 +23,7 @@ _I64 = ctypes.c_int64
 _I32 = ctypes.c_int
 _F32 = ctypes.c_float
 _SZ = ctypes.c_size_t
+_PI64 = ctypes.POINTER(ctypes.c_int64)
 
 
 class NF4Weight(ctypes.Structure):
@@ -63,6 +64,16 @@ SIGNATURES = {
     "sb_ce_backward": (_I32, [_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I32, _P, _SZ, _P]),
     "sb_ce_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sb_ce_check_targets": (_I32, [_P, _I64, _I64, _I64, ctypes.POINTER(_I64), _P]),
+    "sb_rope": (_I32, [_P, _I32, _PI64, _I64, _P, _I32, _P, _I32, _PI64, _I64, _P, _I32, _P, _P, _I32,
+                       _PI64, _PI64, _I64, _I64, _I64, _I64, _I32, _P]),
+    "sb_swiglu_fwd": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P]),
+    "sb_swiglu_bwd": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P]),
+    "sb_nf4_mlp_gate_up_fwd": (_I32, [_P, _I64, ctypes.POINTER(NF4Weight), ctypes.POINTER(NF4Weight), _P, _P,
+                                      _I32, _P, _P, _P]),
+    "sb_nf4_mlp_down_dx": (_I32, [_P, _I64, ctypes.POINTER(NF4Weight), _P, _P, _I32, _P, _P, _P]),
+    "sb_nf4_linear_dx2_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sb_nf4_linear_dx2": (_I32, [_P, _I64, ctypes.POINTER(NF4Weight), ctypes.POINTER(NF4Weight), _P, _P, _I32,
+                                 _P, _P, _SZ, _P]),
 }
 
 _lock = threading.Lock()

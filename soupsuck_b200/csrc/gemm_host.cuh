@@ -125,16 +125,16 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
 constexpr int kPairStages = 6;         // dX, and the stream-K forward
 constexpr int kPairFwdTileStages = 4;  // whole-tile forward (leaves room for store staging)
 
-template <int BMODE, int EMODE, int STAGES, bool SK>
+template <int BMODE, int EMODE, int STAGES, bool SK, int WSEL = 0>
 inline int configure_pair(const char* name) {
-  using C = pair::PairCfg<BMODE, STAGES>;
+  using C = pair::PairCfg<BMODE, STAGES, EMODE>;
   static std::mutex mu;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(pair::pair_kernel<BMODE, EMODE, STAGES, SK>,
+    cudaError_t e = cudaFuncSetAttribute(pair::pair_kernel<BMODE, EMODE, STAGES, SK, WSEL>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " smem attribute: " + cudaGetErrorString(e));
     configured[dev] = true;
@@ -144,7 +144,7 @@ inline int configure_pair(const char* name) {
 
 template <int BMODE, int EMODE, int STAGES>
 inline cudaLaunchConfig_t pair_config(int grid, cudaStream_t stream, cudaLaunchAttribute* attr) {
-  using C = pair::PairCfg<BMODE, STAGES>;
+  using C = pair::PairCfg<BMODE, STAGES, EMODE>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(C::kThreads, 1, 1);
@@ -178,7 +178,7 @@ inline int pair_slots() {
   if (configure_pair<kNF4Fwd, kStoreF16, kPairFwdTileStages, false>("nf4_pair_fwd") == SB_OK) {
     cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = pair_config<kNF4Fwd, kStoreF16, kPairFwdTileStages>(2, nullptr, attr);
-    if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairFwdTileStages, false>, &cfg) !=
+    if (cudaOccupancyMaxActiveClusters(&n, pair::pair_kernel<kNF4Fwd, kStoreF16, kPairFwdTileStages, false, 0>, &cfg) !=
         cudaSuccess) {
       cudaGetLastError();
       n = 0;
@@ -190,24 +190,28 @@ inline int pair_slots() {
   return n;
 }
 
-template <int BMODE, int EMODE, int STAGES, bool SK>
+// b2 / y2: the second weight's packed-code map (gate/up forward) and the second
+// output map (the SwiGLU forward's activation); any valid map otherwise.
+template <int BMODE, int EMODE, int STAGES, bool SK, int WSEL = 0>
 int launch_pair_sk(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
-                   const CUtensorMap& y, Params p, int grid, cudaStream_t stream, const char* name) {
-  if (int rc = configure_pair<BMODE, EMODE, STAGES, SK>(name)) return rc;
+                   const CUtensorMap& y, Params p, int grid, cudaStream_t stream, const char* name,
+                   const CUtensorMap* b2 = nullptr, const CUtensorMap* y2 = nullptr) {
+  if (int rc = configure_pair<BMODE, EMODE, STAGES, SK, WSEL>(name)) return rc;
   if (grid <= 0) return SB_OK;
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pair_config<BMODE, EMODE, STAGES>(grid, stream, attr);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::pair_kernel<BMODE, EMODE, STAGES, SK>, a, b, la, lb, y, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, pair::pair_kernel<BMODE, EMODE, STAGES, SK, WSEL>, a, b, la, lb, y,
+                                     b2 ? *b2 : b, y2 ? *y2 : y, p);
   if (e != cudaSuccess) return fail(SB_ECUDA, std::string(name) + " launch: " + cudaGetErrorString(e));
   count_launch();
   return check_launch(name);
 }
 
-template <int BMODE, int EMODE, int STAGES>
+template <int BMODE, int EMODE, int STAGES, int WSEL = 0>
 int launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
                 const CUtensorMap& y, Params p, int grid, cudaStream_t stream, const char* name) {
-  return p.streamk ? launch_pair_sk<BMODE, EMODE, STAGES, true>(a, b, la, lb, y, p, grid, stream, name)
-                   : launch_pair_sk<BMODE, EMODE, STAGES, false>(a, b, la, lb, y, p, grid, stream, name);
+  return p.streamk ? launch_pair_sk<BMODE, EMODE, STAGES, true, WSEL>(a, b, la, lb, y, p, grid, stream, name)
+                   : launch_pair_sk<BMODE, EMODE, STAGES, false, WSEL>(a, b, la, lb, y, p, grid, stream, name);
 }
 
 // ----------------------------------------------------------------- NF4 linear
@@ -366,6 +370,193 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
     return launch<kNF4Fwd, kStoreF16, kNF4Msub, kNF4BN, kNF4Stages>(ta, tb, tla, tlb, p, stream, "nf4_gemm_fwd");
   }
   return launch<kNF4Dx, kStoreF16, kNF4Msub, kNF4BN, kNF4Stages>(ta, tb, tla, tlb, p, stream, "nf4_gemm_dx");
+}
+
+
+// ----------------------------------------------------------------- Qwen2 MLP (fused SwiGLU)
+// Weight descriptor fields shared by the drivers below.
+inline void set_weight(Params& p, const sb_nf4_weight& w) {
+  p.packed = w.packed;
+  p.qabs = w.qabs;
+  p.absmax2 = w.absmax2;
+  p.code2 = w.code2;
+  p.offset = w.offset;
+  p.w_rows = w.n_out;
+  p.w_cols = w.k_in;
+}
+
+inline void set_second_weight(Params& p, const sb_nf4_weight& w) {
+  p.packed2 = w.packed;
+  p.qabs2 = w.qabs;
+  p.absmax2_2 = w.absmax2;
+  p.code2_2 = w.code2;
+  p.offset2 = w.offset;
+}
+
+inline bool same_shape(const sb_nf4_weight& a, const sb_nf4_weight& b) {
+  return a.n_out == b.n_out && a.k_in == b.k_in;
+}
+
+// gate_up[m, 2N] = [X . deq(Wg)^T | X . deq(Wu)^T] (+ LoRA), act[m, N] = SwiGLU(gate, up):
+// one pair-kernel launch whose tiles hold 128 gate and 128 up columns of the same
+// outputs (rank 0 decodes Wg, rank 1 Wu).  lora_a [m, r] is [s X.Ag^T | s X.Au^T]
+// and lora_b [2N, r] stacks [Bg | 0] over [0 | Bu] (r = 2 x the adapter rank).
+inline int mlp_gate_up(const uint16_t* x, int64_t m, const sb_nf4_weight& wg, const sb_nf4_weight& wu,
+                       const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* gate_up, uint16_t* act,
+                       cudaStream_t stream) {
+  const int64_t n = wg.n_out, k = wg.k_in;
+  const int64_t m_tiles = (m + pair::kTileM - 1) / pair::kTileM, n_tiles = n / pair::kHalfN;
+  CUtensorMap ta, tb, tb2, tla, tlb, ty, ty2;
+  int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m, k * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wg.packed, k / 2, n, k / 2, 32, pair::kHalfN,
+                         CU_TENSOR_MAP_SWIZZLE_32B);
+  if (!rc) rc = make_map(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, wu.packed, k / 2, n, k / 2, 32, pair::kHalfN,
+                         CU_TENSOR_MAP_SWIZZLE_32B);
+  if (!rc) rc = make_map(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, gate_up, 2 * n, m, 4 * n, 64, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_map(&ty2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, n, m, 2 * n, 64, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  tla = ta;
+  tlb = ta;
+  if (r > 0) {
+    rc = make_map(&tla, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_a, r, m, r * 2, r, kTileRows, lora_swizzle(r));
+    if (!rc) rc = make_map(&tlb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_b, r, 2 * n, r * 2, r, pair::kHalfN,
+                           lora_swizzle(r));
+    if (rc) return rc;
+  }
+  Params p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.n_tiles = static_cast<int>(n_tiles);
+  p.k_blocks = static_cast<int>(k / 64);
+  p.lora_r = r;
+  p.store_tma = 1;
+  p.vec_ok = 1;
+  set_weight(p, wg);
+  set_second_weight(p, wu);
+  p.out = gate_up;
+  p.ldo = 2 * n;
+  const int64_t tiles = m_tiles * n_tiles;
+  const int slots = pair_slots();
+  const int grid = 2 * static_cast<int>(tiles < slots ? tiles : slots);
+  return launch_pair_sk<kNF4Fwd, kSwiGLUFwd, kPairFwdTileStages, false, 1>(ta, tb, tla, tlb, ty, p, grid, stream,
+                                                                            "nf4_mlp_gate_up", &tb2, &ty2);
+}
+
+// dgate_up[m, 2N] from the down projection's input gradient: dact = dY . deq(Wd) (+ LoRA,
+// lora_a [m, r], lora_b [N, r]) rounded to fp16, then the SwiGLU derivatives against
+// gate_up[m, 2N] in the epilogue (dgate to [0, N), dup to [N, 2N)).  Whole tiles.
+inline int mlp_down_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight& wd, const uint16_t* lora_a,
+                       const uint16_t* lora_b, int r, const uint16_t* gate_up, uint16_t* dgate_up,
+                       cudaStream_t stream) {
+  const int64_t red = wd.n_out, n = wd.k_in;
+  const int64_t m_tiles = (m + pair::kTileM - 1) / pair::kTileM, n_tiles = (n + pair::kTileN - 1) / pair::kTileN;
+  CUtensorMap ta, tb, tla, tlb, ty;
+  int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dy, red, m, red * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wd.packed, n / 2, red, n / 2, kNF4BN / 2, 64,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!rc) rc = make_map(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dgate_up, 2 * n, m, 4 * n, 64, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  tla = ta;
+  tlb = ta;
+  if (r > 0) {
+    rc = make_map(&tla, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_a, r, m, r * 2, r, kTileRows, lora_swizzle(r));
+    if (!rc) rc = make_map(&tlb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_b, r, n, r * 2, r, pair::kHalfN,
+                           lora_swizzle(r));
+    if (rc) return rc;
+  }
+  Params p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(red);
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.n_tiles = static_cast<int>(n_tiles);
+  p.k_blocks = static_cast<int>((red + 63) / 64);
+  p.lora_r = r;
+  p.store_tma = 1;
+  p.vec_ok = 1;
+  set_weight(p, wd);
+  p.out = dgate_up;
+  p.ldo = 2 * n;
+  p.gu = reinterpret_cast<const __half*>(gate_up);
+  p.ld_gu = 2 * n;
+  const int64_t tiles = m_tiles * n_tiles;
+  const int slots = pair_slots();
+  const int grid = 2 * static_cast<int>(tiles < slots ? tiles : slots);
+  return launch_pair_sk<kNF4Dx, kSwiGLUBwd, kPairStages, false, 0>(ta, tb, tla, tlb, ty, p, grid, stream,
+                                                                    "nf4_mlp_down_dx");
+}
+
+// dX[m, K] = dY2[m, 2N] . [deq(W1); deq(W2)] (+ lora_a [m, r] . lora_b[K, r]^T): the input
+// gradient of two projections of the same input as one reduction of length 2N.
+inline NF4Plan dx2_plan(int64_t m, int64_t n, int64_t k) {
+  NF4Plan pl{};
+  pl.pair = true;
+  pl.m_tiles = (m + pair::kTileM - 1) / pair::kTileM;
+  pl.n_tiles = (k + pair::kTileN - 1) / pair::kTileN;
+  pl.k_blocks = (2 * n + 63) / 64;
+  const int slots = pair_slots();
+  const int64_t tiles = pl.m_tiles * pl.n_tiles;
+  pl.streamk = want_streamk(tiles, pl.k_blocks, slots);
+  const int pairs = pl.streamk ? streamk_grid(tiles, pl.k_blocks, slots) : static_cast<int>(tiles < slots ? tiles : slots);
+  pl.grid = 2 * pairs;
+  pl.workspace = pl.streamk ? align256(static_cast<size_t>(pl.grid) * 2 * pair::kSlotF4 * sizeof(float4)) +
+                                  align256(static_cast<size_t>(tiles) * 2 * sizeof(int))
+                            : 0;
+  return pl;
+}
+
+inline int linear_dx2(const uint16_t* dy2, int64_t m, const sb_nf4_weight& w1, const sb_nf4_weight& w2,
+                      const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* dx, void* workspace,
+                      size_t workspace_bytes, cudaStream_t stream) {
+  const int64_t n = w1.n_out, k = w1.k_in;
+  NF4Plan pl = dx2_plan(m, n, k);
+  if (pl.workspace > 0 && (!workspace || workspace_bytes < pl.workspace)) {
+    return fail(SB_EWORKSPACE, "two-weight dX needs " + std::to_string(pl.workspace) + " workspace bytes");
+  }
+  CUtensorMap ta, tb, tla, tlb, ty;
+  int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dy2, 2 * n, m, 4 * n, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w1.packed, k / 2, n, k / 2, kNF4BN / 2, 64,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!rc) rc = make_map(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dx, k, m, k * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  tla = ta;
+  tlb = ta;
+  if (r > 0) {
+    rc = make_map(&tla, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_a, r, m, r * 2, r, kTileRows, lora_swizzle(r));
+    if (!rc) rc = make_map(&tlb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lora_b, r, k, r * 2, r, pair::kHalfN,
+                           lora_swizzle(r));
+    if (rc) return rc;
+  }
+  Params p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(k);
+  p.K = static_cast<int>(2 * n);
+  p.m_tiles = static_cast<int>(pl.m_tiles);
+  p.n_tiles = static_cast<int>(pl.n_tiles);
+  p.k_blocks = static_cast<int>(pl.k_blocks);
+  p.k_split = static_cast<int>(n / 64);
+  p.lora_r = r;
+  p.store_tma = 1;
+  p.vec_ok = 1;
+  set_weight(p, w1);
+  set_second_weight(p, w2);
+  p.out = dx;
+  p.ldo = k;
+  if (pl.streamk) {
+    p.streamk = 1;
+    p.partials = static_cast<float*>(workspace);
+    p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
+                                        align256(static_cast<size_t>(pl.grid) * 2 * pair::kSlotF4 * sizeof(float4)));
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(pl.m_tiles * pl.n_tiles) * 2 * sizeof(int),
+                                    stream);
+    if (e != cudaSuccess) return fail(SB_ECUDA, std::string("counter reset: ") + cudaGetErrorString(e));
+  }
+  return launch_pair<kNF4Dx, kStoreF16, kPairStages, 2>(ta, tb, tla, tlb, ty, p, pl.grid, stream, "nf4_linear_dx2");
 }
 
 }  // namespace gemm

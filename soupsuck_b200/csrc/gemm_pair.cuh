@@ -45,6 +45,7 @@
 #pragma once
 
 #include "gemm_sm100.cuh"
+#include "swiglu.cuh"
 
 namespace sb {
 namespace gemm {
@@ -101,6 +102,8 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 // Wait until at most one committed store group still reads shared memory.
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Wait until no committed store group still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 // 2-D tiled load into this CTA's shared memory whose byte count completes on the
 // rank-0 CTA's mbarrier `leader_bar` (a shared::cluster address).  No multicast.
@@ -170,7 +173,7 @@ constexpr int kHalfN = 128;   // B rows (output columns) each CTA decodes per ti
 constexpr int kTileN = 256;   // output columns per pair tile
 constexpr int kTileM = 256;   // output rows per pair tile (128 per CTA)
 
-template <int BMODE, int STAGES>
+template <int BMODE, int STAGES, int EMODE = kStoreF16>
 struct PairCfg {
   static constexpr bool kBMN = (BMODE == kNF4Dx);
   static constexpr int kABytes = kTileRows * kBK * 2;      // 16 KB
@@ -187,14 +190,18 @@ struct PairCfg {
   static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
   static constexpr int kThreads = 512;
   static constexpr int kBarrierBytes = 1024 + 1024;        // barriers + the code2 table
-  // Epilogue staging: per epilogue warp two 32-row x 64-column fp16 boxes (SW128).
+  // Epilogue staging: per epilogue warp two 32-row x 64-column fp16 boxes (SW128);
+  // three for the SwiGLU forward, whose panels go out as gate, up and activation.
   static constexpr int kStoreBoxBytes = 32 * 64 * 2;
-  static constexpr int kStagingBytes = kStoreStage ? 4 * 2 * kStoreBoxBytes : 0;
+  static constexpr int kBoxes = EMODE == kSwiGLUFwd ? 3 : 2;
+  static constexpr int kStagingBytes = kStoreStage ? 4 * kBoxes * kStoreBoxBytes : 0;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + kBarrierBytes + 1024;
   static_assert(STAGES % 2 == 0, "two decoder groups alternate stages: each stage keeps one group");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kSmemBytes > 232448 / 2, "one CTA per SM keeps TMEM allocation uncontended");
   static_assert(BMODE == kNF4Fwd || BMODE == kNF4Dx, "NF4 operand modes only");
+  static_assert(EMODE != kSwiGLUFwd || (BMODE == kNF4Fwd && kStoreStage), "SwiGLU forward: staged forward");
+  static_assert(EMODE != kSwiGLUBwd || BMODE == kNF4Dx, "SwiGLU backward: dX epilogue");
 };
 
 // Stream-K partial slot of one CTA: [chunk 8][float4 8][thread 128], 128 KB.
@@ -205,7 +212,8 @@ constexpr int kSlotF4 = (kTileN / 32) * 8 * 128;
 // columns of the tile.  Releases go to rank 0's acc_empty.
 // STAGE: the kernel has store staging (bulk-store epilogue available).
 template <int EMODE, bool SK, bool STAGE>
-__device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap* tmY, uint8_t* staging,
+__device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap* tmY, const CUtensorMap* tmY2,
+                                              uint8_t* staging,
                                               uint32_t tmem_base, uint64_t* acc_full,
                                               uint32_t leader_acc_empty, uint64_t* epi_mb,
                                               volatile int* abort_flag, volatile int* last_flag, int warp,
@@ -216,8 +224,9 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
   const int64_t total = static_cast<int64_t>(num_tiles) * p.k_blocks;
   uint32_t tl = 0, epi_phase = 0, boxes = 0;
   int uidx = 0;
-  // This warp's two staging boxes; rows of a box are this warp's 32 TMEM lanes.
-  uint8_t* my_boxes = staging + (warp - 4) * 2 * (32 * 64 * 2);
+  // This warp's staging boxes; rows of a box are this warp's 32 TMEM lanes.
+  constexpr int kBoxes = EMODE == kSwiGLUFwd ? 3 : 2;
+  uint8_t* my_boxes = staging + (warp - 4) * kBoxes * (32 * 64 * 2);
   UnitIter iter(p, num_tiles, pair_id, pairs);
   Unit u;
   while (iter.next(u)) {
@@ -230,7 +239,122 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
     tc_fence_after();
     const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kTileN;
     const int row = m0 + static_cast<int>(rank) * kTileRows + q * 32 + lane;
-    if (STAGE && (!SK || (u.k0 == 0 && u.k1 == p.k_blocks)) && p.store_tma) {
+    if constexpr (EMODE == kSwiGLUFwd) {
+      // Gate/up tile: accumulator columns [0, 128) are gate and [128, 256) up for
+      // output columns nt*128 .. +128.  Per 64-column panel the warp stages fp16
+      // gate, up and act = SwiGLU(gate, up) (computed from the rounded gate/up, as
+      // the reference's element-wise kernel sees them) and stores the three boxes:
+      // gate and up into the [M, 2N] buffer (up at column N + c), act into [M, N].
+      const int row0 = m0 + static_cast<int>(rank) * kTileRows + q * 32;
+      const int oc0 = nt * kHalfN;
+      const uint32_t swz = static_cast<uint32_t>(lane & 7);
+      uint8_t* box_g = my_boxes;
+      uint8_t* box_u = my_boxes + 32 * 64 * 2;
+      uint8_t* box_a = my_boxes + 2 * 32 * 64 * 2;
+#pragma unroll 1
+      for (int panel = 0; panel < kHalfN / 64; ++panel) {
+        // The previous panel's stores must have finished reading the three boxes.
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t vg[32], vu[32];
+          tmem_ld32(tacc + panel * 64 + half * 32, vg);
+          tmem_ld32(tacc + kHalfN + panel * 64 + half * 32, vu);
+          tmem_ld_wait();
+          uint32_t hg[16], hu[16], ha[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            __half2 g2 = __floats2half2_rn(__uint_as_float(vg[2 * j]), __uint_as_float(vg[2 * j + 1]));
+            __half2 u2 = __floats2half2_rn(__uint_as_float(vu[2 * j]), __uint_as_float(vu[2 * j + 1]));
+            const float2 gf = __half22float2(g2), uf = __half22float2(u2);
+            __half2 a2 = __floats2half2_rn(swiglu::forward(gf.x, uf.x), swiglu::forward(gf.y, uf.y));
+            hg[j] = *reinterpret_cast<uint32_t*>(&g2);
+            hu[j] = *reinterpret_cast<uint32_t*>(&u2);
+            ha[j] = *reinterpret_cast<uint32_t*>(&a2);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t off = lane * 128 + ((static_cast<uint32_t>(half * 4 + c) ^ swz) << 4);
+            *reinterpret_cast<uint4*>(box_g + off) = make_uint4(hg[4 * c], hg[4 * c + 1], hg[4 * c + 2], hg[4 * c + 3]);
+            *reinterpret_cast<uint4*>(box_u + off) = make_uint4(hu[4 * c], hu[4 * c + 1], hu[4 * c + 2], hu[4 * c + 3]);
+            *reinterpret_cast<uint4*>(box_a + off) = make_uint4(ha[4 * c], ha[4 * c + 1], ha[4 * c + 2], ha[4 * c + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmY, box_g, oc0 + panel * 64, row0);
+          tma_store_2d(tmY, box_u, p.N + oc0 + panel * 64, row0);
+          tma_store_2d(tmY2, box_a, oc0 + panel * 64, row0);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+    } else if constexpr (EMODE == kSwiGLUBwd) {
+      // Down-projection dX tile: the accumulator is dL/d(act) for columns
+      // n0 .. n0+256 of this CTA's 128 rows.  Rounded to fp16 (the down
+      // projection's input-gradient dtype), it meets the saved gate / up values
+      // of the same positions; dgate goes to columns [0, N) and dup to [N, 2N)
+      // of the [M, 2N] output.  Rows past M read nothing (their stores are
+      // clipped by the tensor map); N is a multiple of 64.
+      const int row0 = m0 + static_cast<int>(rank) * kTileRows + q * 32;
+      const uint32_t swz = static_cast<uint32_t>(lane & 7);
+      uint8_t* box_dg = my_boxes;
+      uint8_t* box_du = my_boxes + 32 * 64 * 2;
+      const bool row_ok = row < p.M;
+      const __half* grow = p.gu + static_cast<int64_t>(row_ok ? row : 0) * p.ld_gu;
+#pragma unroll 1
+      for (int panel = 0; panel < kTileN / 64; ++panel) {
+        const int c_panel = n0 + panel * 64;
+        if (c_panel >= p.N) break;
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          const int c0 = c_panel + half * 32;
+          uint32_t v[32];
+          tmem_ld32(tacc + panel * 64 + half * 32, v);
+          uint4 gw[4], uw[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            gw[c] = row_ok ? __ldg(reinterpret_cast<const uint4*>(grow + c0) + c) : make_uint4(0, 0, 0, 0);
+            uw[c] = row_ok ? __ldg(reinterpret_cast<const uint4*>(grow + p.N + c0) + c) : make_uint4(0, 0, 0, 0);
+          }
+          tmem_ld_wait();
+          const __half2* g2 = reinterpret_cast<const __half2*>(gw);
+          const __half2* u2 = reinterpret_cast<const __half2*>(uw);
+          uint32_t hdg[16], hdu[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float2 da = __half22float2(__floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
+            const float2 gf = __half22float2(g2[j]), uf = __half22float2(u2[j]);
+            float dg0, du0, dg1, du1;
+            swiglu::backward(gf.x, uf.x, da.x, dg0, du0);
+            swiglu::backward(gf.y, uf.y, da.y, dg1, du1);
+            __half2 dg = __floats2half2_rn(dg0, dg1), du = __floats2half2_rn(du0, du1);
+            hdg[j] = *reinterpret_cast<uint32_t*>(&dg);
+            hdu[j] = *reinterpret_cast<uint32_t*>(&du);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t off = lane * 128 + ((static_cast<uint32_t>(half * 4 + c) ^ swz) << 4);
+            *reinterpret_cast<uint4*>(box_dg + off) = make_uint4(hdg[4 * c], hdg[4 * c + 1], hdg[4 * c + 2], hdg[4 * c + 3]);
+            *reinterpret_cast<uint4*>(box_du + off) = make_uint4(hdu[4 * c], hdu[4 * c + 1], hdu[4 * c + 2], hdu[4 * c + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmY, box_dg, c_panel, row0);
+          tma_store_2d(tmY, box_du, p.N + c_panel, row0);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+    } else if (STAGE && (!SK || (u.k0 == 0 && u.k1 == p.k_blocks)) && p.store_tma) {
       // fp32 (+ bias) -> fp16, staged per 64-column panel into a 128B-swizzled box
       // and written by one bulk tensor store: every global write is a full
       // 128-byte row segment instead of 32 scattered 16-byte pieces per warp store.
@@ -386,12 +510,15 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
 // ------------------------------------------------------------ the kernel
 // SK: stream-K schedule (partial tiles and their fix-up); the whole-tile
 // instantiation carries no fix-up code, which keeps it free of register spills.
-template <int BMODE, int EMODE, int STAGES, bool SK>
-__global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
+template <int BMODE, int EMODE, int STAGES, bool SK, int WSEL>
+__global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
     pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
-                const __grid_constant__ CUtensorMap tmY, const Params p) {
-  using C = PairCfg<BMODE, STAGES>;
+                const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmB2,
+                const __grid_constant__ CUtensorMap tmY2, const Params p) {
+  using C = PairCfg<BMODE, STAGES, EMODE>;
+  static_assert(WSEL == 0 || (WSEL == 1 && BMODE == kNF4Fwd && !SK) || (WSEL == 2 && BMODE == kNF4Dx),
+                "weight selection: 1 = gate/up forward (whole tiles), 2 = two-weight dX");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * C::kStageBytes;
@@ -446,7 +573,11 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
   // before that kernel has completed and its writes are visible.
   grid_dependency_wait();
   launch_dependents();
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) code2_s[i] = __ldg(p.code2 + i);
+  {
+    // The decoders' scale table: the second weight's for the rank-1 CTA of a gate/up pair.
+    const float* table = (WSEL == 1 && rank == 1) ? p.code2_2 : p.code2;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) code2_s[i] = __ldg(table + i);
+  }
   __syncthreads();
   const uint32_t tmem_base = *tmem_holder;
   const int rows_valid = runtime_rows(p);
@@ -459,7 +590,9 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
-      if (C::kRawTma) tma_prefetch_desc(&tmB);
+      // Gate/up pairing: the rank-1 CTA loads the second weight's packed codes.
+      const CUtensorMap* bmap = (WSEL == 1 && rank == 1) ? &tmB2 : &tmB;
+      if (C::kRawTma) tma_prefetch_desc(bmap);
       if (has_lora) {
         tma_prefetch_desc(&tmLA);
         tma_prefetch_desc(&tmLB);
@@ -473,7 +606,10 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
         const int m0 = mt * kTileM;
         if (m0 >= rows_valid) continue;
         const int arow = m0 + static_cast<int>(rank) * kTileRows;
-        const int brow = nt * kTileN + static_cast<int>(rank) * kHalfN;
+        // A gate/up tile covers output columns nt*128.. of both weights; its LoRA B
+        // rows come from the [2N, r] stack of both weights' factors.
+        const int brow = WSEL == 1 ? nt * kHalfN : nt * kTileN + static_cast<int>(rank) * kHalfN;
+        const int lbrow = WSEL == 1 ? static_cast<int>(rank) * p.N + nt * kHalfN : brow;
         const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
         for (int ls = 0; ls < nsteps; ++ls, ++it) {
           const int s = it % STAGES;
@@ -487,12 +623,12 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
             tma_load_2d_pair(a_s, &tmA, leader_full + 8u * s, step * kBK, arow);
             if constexpr (C::kRawTma) {
               mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
-              tma_load_2d(b_s + C::kBBytes, &tmB, &raw_full[s], step * (kBK / 2), brow);
+              tma_load_2d(b_s + C::kBBytes, bmap, &raw_full[s], step * (kBK / 2), brow);
             }
           } else {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * (kTileRows + kHalfN) * p.lora_r * 2);
             tma_load_2d_pair(a_s, &tmLA, leader_full + 8u * s, 0, arow);
-            tma_load_2d_pair(b_s, &tmLB, leader_full + 8u * s, 0, brow);
+            tma_load_2d_pair(b_s, &tmLB, leader_full + 8u * s, 0, lbrow);
             if constexpr (C::kRawTma) mbar_arrive(&raw_full[s]);  // nothing to decode
           }
         }
@@ -577,7 +713,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
     }
   } else if (warp >= 4 && warp < 8) {
     if (lane == 0 && C::kStoreStage && p.store_tma) tma_prefetch_desc(&tmY);
-    pair_epilogue<EMODE, SK, C::kStoreStage>(p, &tmY, staging, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
+    if (lane == 0 && EMODE == kSwiGLUFwd) tma_prefetch_desc(&tmY2);
+    pair_epilogue<EMODE, SK, C::kStoreStage>(p, &tmY, &tmY2, staging, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
                          num_tiles, rows_valid, pair_id, pairs, rank);
   } else if (warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders (both CTAs)
@@ -589,49 +726,74 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
     // that read it has completed.
     const int group = (warp - 8) >> 2;
     const int gtid = ((warp - 8) & 3) * 32 + lane;
-    const float off = __ldg(p.offset);
+    // The weight a reduction step decodes: the only one (WSEL 0), this CTA's half
+    // of a gate/up pair (WSEL 1), or the first / second of a concatenated
+    // reduction (WSEL 2, steps >= k_split belong to the second, counted from 0).
+    struct WView {
+      const uint8_t* packed;
+      const uint8_t* qabs;
+      const float* absmax2;
+      float off;
+    };
+    const WView first_w{p.packed, p.qabs, p.absmax2, __ldg(p.offset)};
+    WView second_w = first_w;
+    if constexpr (WSEL != 0) second_w = WView{p.packed2, p.qabs2, p.absmax2_2, __ldg(p.offset2)};
+    const WView own_w = (WSEL == 1 && rank == 1) ? second_w : first_w;
+    // A second weight's scale table is the shared-memory one when both weights
+    // name the same table (bitsandbytes' dynamic map), else read through L1.
+    const bool own_table = WSEL != 2 || p.code2_2 == p.code2;
+    auto in_second = [&](int step) -> bool { return WSEL == 2 && step >= p.k_split; };
+    auto local_step = [&](int step) -> int { return in_second(step) ? step - p.k_split : step; };
+    auto view_of = [&](int step) -> const WView& { return in_second(step) ? second_w : own_w; };
     const int64_t bpr = p.w_cols / 64;
     const int64_t pitch = p.w_cols / 2;  // packed bytes per weight row
     uint32_t it = 0;
     bool ok = true;
-    // Block index of this thread's (row, 64-block) at k-step `step`, or -1 outside the weight.
+    // Block index of this thread's (row, 64-block) at k-step `step` (within the
+    // weight that step reads), or -1 outside the weight.
     auto block_of = [&](int n0, int step) -> int64_t {
+      const int ls = local_step(step);
       if constexpr (BMODE == kNF4Fwd) {
         const int64_t wrow = n0 + gtid;
-        return wrow < p.w_rows ? wrow * bpr + step : -1;
+        return wrow < p.w_rows ? wrow * bpr + ls : -1;
       } else {
-        const int64_t wrow = static_cast<int64_t>(step) * kBK + (gtid >> 1);
+        const int64_t wrow = static_cast<int64_t>(ls) * kBK + (gtid >> 1);
         const int64_t wcol = n0 + 64 * (gtid & 1);
         return (wrow < p.w_rows && wcol < p.w_cols) ? wrow * bpr + wcol / 64 : -1;
       }
     };
     // Byte offset of that block's packed codes (row-major packing, 32 bytes per block).
     auto bytes_of = [&](int n0, int step) -> int64_t {
+      const int ls = local_step(step);
       if constexpr (BMODE == kNF4Fwd) {
-        return static_cast<int64_t>(n0 + gtid) * pitch + step * (kBK / 2);
+        return static_cast<int64_t>(n0 + gtid) * pitch + ls * (kBK / 2);
       } else {
-        return (static_cast<int64_t>(step) * kBK + (gtid >> 1)) * pitch + (n0 + 64 * (gtid & 1)) / 2;
+        return (static_cast<int64_t>(ls) * kBK + (gtid >> 1)) * pitch + (n0 + 64 * (gtid & 1)) / 2;
       }
     };
     UnitIter iter(p, num_tiles, pair_id, pairs);
     Unit u;
     while (ok && iter.next(u)) {
       if ((u.tile % p.m_tiles) * kTileM >= rows_valid) continue;
-      const int n0 = (u.tile / p.m_tiles) * kTileN + static_cast<int>(rank) * kHalfN;
+      const int nt = u.tile / p.m_tiles;
+      const int n0 = WSEL == 1 ? nt * kHalfN : nt * kTileN + static_cast<int>(rank) * kHalfN;
       const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
       const int first = u.k0 + ((static_cast<int>(it & 1) == group) ? 0 : 1);
       int64_t nb = first < u.k1 ? block_of(n0, first) : -1;
       uint4 w0_next = make_uint4(0, 0, 0, 0), w1_next = make_uint4(0, 0, 0, 0);
       uint32_t q_next = 0u;
       float a2_next = 0.0f;
+      bool second_next = false;
       if (nb >= 0) {
+        const WView& wv = view_of(first);
         if constexpr (!C::kRawTma) {
-          const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, first));
+          const uint4* src = reinterpret_cast<const uint4*>(wv.packed + bytes_of(n0, first));
           w0_next = ld_stream16(src);
           w1_next = ld_stream16(src + 1);
         }
-        q_next = __ldg(p.qabs + nb);
-        a2_next = __ldg(p.absmax2 + (nb >> 8));
+        q_next = __ldg(wv.qabs + nb);
+        a2_next = __ldg(wv.absmax2 + (nb >> 8));
+        second_next = in_second(first);
       }
       for (int ls = 0; ls < nsteps; ++ls, ++it) {
         if (static_cast<int>(it & 1) != group) continue;
@@ -642,16 +804,19 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
         const uint4 w0 = w0_next, w1 = w1_next;
         const uint32_t q_cur = q_next;
         const float a2_cur = a2_next;
+        const bool second_cur = second_next;
         const bool valid = main_step && block_of(n0, step) >= 0;
         nb = step + 2 < u.k1 ? block_of(n0, step + 2) : -1;
         if (nb >= 0) {
+          const WView& wv = view_of(step + 2);
           if constexpr (!C::kRawTma) {
-            const uint4* src = reinterpret_cast<const uint4*>(p.packed + bytes_of(n0, step + 2));
+            const uint4* src = reinterpret_cast<const uint4*>(wv.packed + bytes_of(n0, step + 2));
             w0_next = ld_stream16(src);
             w1_next = ld_stream16(src + 1);
           }
-          q_next = __ldg(p.qabs + nb);
-          a2_next = __ldg(p.absmax2 + (nb >> 8));
+          q_next = __ldg(wv.qabs + nb);
+          a2_next = __ldg(wv.absmax2 + (nb >> 8));
+          second_next = in_second(step + 2);
         }
         // Forward: raw_full[s] (the producer loaded the packed codes after empty[s]).
         // dX: empty[s] (the UMMA that read this B slot has completed).
@@ -662,7 +827,11 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES>::kThreads, 1)
         }
         if (main_step) {
           uint8_t* b_s = smem + s * C::kStageBytes + C::kABytes;
-          const float scale = valid ? __fadd_rn(__fmul_rn(code2_s[q_cur], a2_cur), off) : 0.0f;
+          float scale = 0.0f;
+          if (valid) {
+            const float code = (!second_cur || own_table) ? code2_s[q_cur] : __ldg(p.code2_2 + q_cur);
+            scale = __fadd_rn(__fmul_rn(code, a2_cur), second_cur ? second_w.off : own_w.off);
+          }
           if constexpr (C::kRawTma) {
             // Packed rows are 32 B, TMA-swizzled in 32 B spans: chunk ^= (row >> 2) & 1.
             const uint8_t* raw_s = b_s + C::kBBytes;

@@ -36,7 +36,10 @@ namespace sb {
 namespace gemm {
 
 enum BMode : int { kNF4Fwd = 0, kNF4Dx = 1, kDenseK = 2, kDenseMN = 3 };
-enum EMode : int { kStoreF16 = 0, kStoreF32 = 1, kAccF32 = 2, kCeStats = 3, kCeDz = 4 };
+enum EMode : int { kStoreF16 = 0, kStoreF32 = 1, kAccF32 = 2, kCeStats = 3, kCeDz = 4,
+                   // 2-SM pair kernel only (gemm_pair.cuh): the Qwen2 MLP's SwiGLU fused into
+                   // the gate/up forward and into the down projection's dX
+                   kSwiGLUFwd = 5, kSwiGLUBwd = 6 };
 
 constexpr int kBK = 64;        // reduction elements per pipeline stage (one 128 B swizzle row)
 constexpr int kTileRows = 128; // rows per UMMA (M = 128, cta_group::1)
@@ -62,6 +65,19 @@ struct Params {
   const float* offset;
   int64_t w_rows;          // n_out of the weight
   int64_t w_cols;          // k_in of the weight
+  // A second NF4 weight of the same shape (2-SM pair kernel, WSEL != 0):
+  //   WSEL 1, gate/up forward: a pair tile's rank-1 CTA decodes this weight's rows
+  //           [nt*128, nt*128 + 128) while rank 0 decodes the first weight's;
+  //   WSEL 2, concatenated dX: reduction blocks >= k_split decode this weight.
+  const uint8_t* packed2;
+  const uint8_t* qabs2;
+  const float* absmax2_2;
+  const float* code2_2;
+  const float* offset2;
+  int k_split;
+  // kSwiGLUBwd: the MLP's [M, 2N] gate (columns [0, N)) / up ([N, 2N)) buffer.
+  const __half* gu;
+  int64_t ld_gu;
   // epilogue
   void* out;
   int64_t ldo;

@@ -9,3 +9,6 @@
 #include "lora_mma.cuh"
 #include "lora_static.cuh"
 #include "cross_entropy.cuh"
+#include "rope.cuh"
+#include "swiglu.cuh"
+#include "mlp.cuh"

@@ -225,13 +225,13 @@ class _VocabShardCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden, weight_rows, targets, v0, v1, ignore_index, group):
         from . import _lib
-        from .kernels.cross_entropy import _pad_h
+        from .kernels.cross_entropy import _half_padded
 
         n, h = hidden.shape
         v = weight_rows.shape[0]
         h8 = (h + 7) // 8 * 8
-        hidden16 = _pad_h(hidden.to(torch.float16), h8)
-        weight16 = _pad_h(weight_rows.to(torch.float16), h8)
+        hidden16 = _half_padded(hidden, h8)
+        weight16 = _half_padded(weight_rows, h8)
         tloc, inside = local_targets(targets, v0, v1, ignore_index)
         tloc = tloc.contiguous()
         f32 = dict(device=hidden.device, dtype=torch.float32)

@@ -1,0 +1,221 @@
+"""The Qwen2 MLP on NF4 weights with SwiGLU inside the GEMM epilogues
+(reference: the frozen MLP boundary solution/mlp.py:500-593 and the SwiGLU tile
+engine solution/kernels/swiglu_fused.py:21-78).
+
+    gate, up = X.deq(Wg)^T + s(X.Ag^T).Bg^T,  X.deq(Wu)^T + s(X.Au^T).Bu^T
+    act      = SwiGLU(gate, up) = gate * sigmoid(gate) * up          (fp32 math on fp16 gate/up)
+    Y        = act.deq(Wd)^T + s(act.Ad^T).Bd^T
+
+Forward: ONE pair-kernel launch computes gate and up together -- each 256-wide
+tile holds 128 gate and the same 128 up columns (one CTA of the pair decodes
+Wg, the other Wu) -- and its epilogue writes gate|up [T, 2N] (kept for the
+backward) and act [T, N]; then the down projection.  Backward: the down
+projection's dX kernel applies the SwiGLU derivatives in its epilogue against
+the saved gate|up and writes dgate|dup [T, 2N]; the gate and up input gradients
+are ONE GEMM whose reduction runs over both weights (dX = dgate.Wg + dup.Wu),
+with both LoRA terms as one rank-2r step.  The LoRA factors of gate and up
+travel as one rank-2r pair (block-diagonal where they must not mix), so their
+projections and weight-gradient reductions are one launch each.
+
+``swiglu_fused_forward`` / ``swiglu_fused_backward`` keep the reference's
+element-wise API (sb_swiglu_fwd / sb_swiglu_bwd) for gate/up tensors that come
+from elsewhere.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import weakref
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from .. import _lib
+from .._spec import HALF, Operand, admit, refuse
+from .nf4 import nested_shape
+from .nf4_gemm import (_factors, _padded_rank, _project, _reduce, _weight_struct, nf4_linear_raw)
+
+
+# ------------------------------------------------------------------ element-wise SwiGLU
+def _matrix(t):
+    return t.reshape(-1, t.shape[-1]) if t.ndim != 2 else t
+
+
+def swiglu_fused_forward(gate, up, out=None):
+    """act = gate * sigmoid(gate) * up for fp16 CUDA tensors of one shape (last
+    dimension unit-strided); fills ``out`` when given."""
+    admit("swiglu_fused_forward", gate.device if isinstance(gate, torch.Tensor) else None,
+          gate=(gate, Operand(HALF, layout="rows")), up=(up, Operand(HALF, layout="rows")),
+          out=(out, Operand(HALF, layout="rows", optional=True)))
+    if gate.shape != up.shape or (out is not None and out.shape != gate.shape):
+        refuse("swiglu_fused_forward", "gate, up and out must have one shape")
+    if out is None:
+        out = torch.empty_like(gate, memory_format=torch.contiguous_format)
+    g, u, a = _matrix(gate), _matrix(up), _matrix(out)
+    if g.numel():
+        with torch.cuda.device(gate.device):
+            _lib.call("sb_swiglu_fwd", g.data_ptr(), g.stride(0), u.data_ptr(), u.stride(0), a.data_ptr(),
+                      a.stride(0), g.shape[0], g.shape[1], _lib.stream_of(gate.device))
+    return out
+
+
+def swiglu_fused_backward(gate, up, grad, gate_dtype=None, up_dtype=None):
+    """(dgate, dup) of act = SwiGLU(gate, up) for the upstream ``grad`` (fp16)."""
+    admit("swiglu_fused_backward", gate.device if isinstance(gate, torch.Tensor) else None,
+          gate=(gate, Operand(HALF, layout="rows")), up=(up, Operand(HALF, layout="rows")),
+          grad=(grad, Operand(HALF, layout="rows")))
+    if gate.shape != up.shape or grad.shape != gate.shape:
+        refuse("swiglu_fused_backward", "gate, up and grad must have one shape")
+    if gate_dtype not in (None, HALF) or up_dtype not in (None, HALF):
+        refuse("swiglu_fused_backward", "the derivatives are produced in fp16")
+    dgate = torch.empty(gate.shape, device=gate.device, dtype=HALF)
+    dup = torch.empty(gate.shape, device=gate.device, dtype=HALF)
+    g, u, d, dg, du = (_matrix(t) for t in (gate, up, grad, dgate, dup))
+    if g.numel():
+        with torch.cuda.device(gate.device):
+            _lib.call("sb_swiglu_bwd", g.data_ptr(), g.stride(0), u.data_ptr(), u.stride(0), d.data_ptr(),
+                      d.stride(0), dg.data_ptr(), dg.stride(0), du.data_ptr(), du.stride(0), g.shape[0],
+                      g.shape[1], _lib.stream_of(gate.device))
+    return dgate, dup
+
+
+# ------------------------------------------------------------------ gate/up LoRA as one rank-2r pair
+class _PairFactors:
+    """The gate and up adapters as one rank-2r adapter (rp = padded rank):
+    a_cat [2rp, H] (both A stacked), at_cat [H, 2rp], b_gu [2N, 2rp] = [Bg 0; 0 Bu],
+    bt_bd [2rp, 2N] = [Bg^T 0; 0 Bu^T]."""
+
+    def __init__(self, fg, fu):
+        rp, n = fg.rp, fg.b16.shape[0]
+        dev = fg.a16.device
+        self.rp, self.r_gate, self.r_up = rp, fg.r, fu.r
+        self.a_cat = torch.cat([fg.a16, fu.a16])
+        self.at_cat = torch.cat([fg.at16, fu.at16], dim=1)
+        self.b_gu = torch.zeros((2 * n, 2 * rp), device=dev, dtype=HALF)
+        self.b_gu[:n, :rp] = fg.b16
+        self.b_gu[n:, rp:] = fu.b16
+        self.bt_bd = torch.zeros((2 * rp, 2 * n), device=dev, dtype=HALF)
+        self.bt_bd[:rp, :n] = fg.bt16
+        self.bt_bd[rp:, n:] = fu.bt16
+
+
+_PAIR_CACHE = {}
+
+
+def _pair_factors(ag, bg, au, bu):
+    fg, fu = _factors(ag, bg), _factors(au, bu)
+    if torch.cuda.is_current_stream_capturing():
+        return _PairFactors(fg, fu)
+    key = (id(fg), id(fu))
+    hit = _PAIR_CACHE.get(key)
+    if hit is not None and hit[0]() is fg and hit[1]() is fu:
+        return hit[2]
+    pf = _PairFactors(fg, fu)
+    if len(_PAIR_CACHE) > 1024:
+        _PAIR_CACHE.clear()
+    _PAIR_CACHE[key] = (weakref.ref(fg), weakref.ref(fu), pf)
+    return pf
+
+
+class _FusedMLP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, scaling, g_packed, g_state, ag, bg, u_packed, u_state, au, bu, d_packed, d_state, ad, bd):
+        n, h = g_state.shape
+        x2d = x.reshape(-1, h)
+        if not x2d.is_contiguous():
+            x2d = x2d.contiguous()
+        t = x2d.shape[0]
+        dev = x.device
+        pf = _pair_factors(ag, bg, au, bu)
+        fd = _factors(ad, bd)
+        s = float(scaling)
+        stream = _lib.stream_of(dev)
+        z_rows, z_t = _project(x2d, pf.a_cat, 2 * pf.rp, s, True, 1.0, True)
+        gate_up = torch.empty((t, 2 * n), device=dev, dtype=HALF)
+        act = torch.empty((t, n), device=dev, dtype=HALF)
+        wg, wu = _weight_struct(g_packed, g_state), _weight_struct(u_packed, u_state)
+        if t:
+            _lib.call("sb_nf4_mlp_gate_up_fwd", x2d.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
+                      z_rows.data_ptr(), pf.b_gu.data_ptr(), 2 * pf.rp, gate_up.data_ptr(), act.data_ptr(),
+                      stream)
+        zd_rows, zd_t = _project(act, fd.a16, fd.rp, s, True, 1.0, True)
+        y = nf4_linear_raw(act, d_packed, d_state, lora_a=zd_rows, lora_b=fd.b16)
+        ctx.save_for_backward(x2d, gate_up, act, z_t, zd_t, pf.at_cat, pf.bt_bd, fd.at16, fd.bt16,
+                              g_packed, u_packed, d_packed)
+        ctx.states = (g_state, u_state, d_state)
+        ctx.meta = (s, pf.rp, pf.r_gate, pf.r_up, fd.r, x.shape, ag.dtype, bg.dtype, au.dtype, bu.dtype,
+                    ad.dtype, bd.dtype)
+        return y.reshape(*x.shape[:-1], d_state.shape[0])
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad):
+        (x2d, gate_up, act, z_t, zd_t, at_cat, bt_bd, at_d, bt_d, g_packed, u_packed, d_packed) = ctx.saved_tensors
+        g_state, u_state, d_state = ctx.states
+        s, rp, r_gate, r_up, r_down, x_shape, ag_t, bg_t, au_t, bu_t, ad_t, bd_t = ctx.meta
+        n, h = g_state.shape
+        hd = d_state.shape[0]
+        g = grad.reshape(-1, hd)
+        if g.dtype != HALF or not g.is_contiguous():
+            g = g.to(HALF).contiguous()
+        t = g.shape[0]
+        dev = g.device
+        stream = _lib.stream_of(dev)
+        # down: rank-r factor of its input gradient, then dact -> (dgate, dup) in one launch
+        rpd = at_d.shape[1]
+        ud, ud_t = _project(g, bt_d, rpd, s, True, s, True)
+        dgate_up = torch.empty((t, 2 * n), device=dev, dtype=HALF)
+        wd = _weight_struct(d_packed, d_state)
+        if t:
+            _lib.call("sb_nf4_mlp_down_dx", g.data_ptr(), t, ctypes.byref(wd), ud.data_ptr(), at_d.data_ptr(),
+                      rpd, gate_up.data_ptr(), dgate_up.data_ptr(), stream)
+        d_ad = _reduce(ud_t, act, rpd, 1.0, False, ad_t)[:r_down]
+        d_bd = _reduce(zd_t, g, rpd, s, True, bd_t)[:, :r_down]
+        # gate + up: one reduction over both weights, both LoRA terms in one rank-2rp step
+        u_cat, u_cat_t = _project(dgate_up, bt_bd, 2 * rp, s, True, s, True)
+        dx = torch.empty((t, h), device=dev, dtype=HALF)
+        wg, wu = _weight_struct(g_packed, g_state), _weight_struct(u_packed, u_state)
+        if t:
+            nbytes = _lib.query("sb_nf4_linear_dx2_workspace_bytes", t, n, h)
+            scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+            _lib.call("sb_nf4_linear_dx2", dgate_up.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
+                      u_cat.data_ptr(), at_cat.data_ptr(), 2 * rp, dx.data_ptr(), scratch.data_ptr(), nbytes,
+                      stream)
+        d_acat = _reduce(u_cat_t, x2d, 2 * rp, 1.0, False, torch.float32)
+        d_bgu = _reduce(z_t, dgate_up, 2 * rp, s, True, torch.float32)
+        d_ag = d_acat[:r_gate].to(ag_t)
+        d_au = d_acat[rp:rp + r_up].to(au_t)
+        d_bg = d_bgu[:n, :r_gate].to(bg_t)
+        d_bu = d_bgu[n:, rp:rp + r_up].to(bu_t)
+        return (dx.reshape(x_shape), None, None, None, d_ag, d_bg, None, None, d_au, d_bu, None, None,
+                d_ad, d_bd)
+
+
+def nf4_swiglu_mlp(x, gate, up, down, scaling=1.0):
+    """Differentiable Qwen2 MLP ``down(SwiGLU(gate(x), up(x)))`` on NF4 weights with
+    LoRA on every projection.  x: fp16 [..., H] CUDA; gate / up / down: tuples
+    (packed, quant_state, lora_a [r, in], lora_b [out, r]) with gate/up [N, H] and
+    down [H, N]; N a multiple of 128, H and N multiples of 64; adapter ranks <= 32.
+    Returns fp16 [..., H]."""
+    entry = "nf4_swiglu_mlp"
+    (gp, gs, ag, bg), (up_p, us, au, bu), (dp, ds, ad, bd) = gate, up, down
+    n, h = nested_shape(gp, gs, entry=entry)
+    if nested_shape(up_p, us, entry=entry) != (n, h) or nested_shape(dp, ds, entry=entry) != (h, n):
+        refuse(entry, "gate/up must be [N, H] and down [H, N]")
+    if n % 128 or h % 64:
+        refuse(entry, f"intermediate size {n} must be a multiple of 128 and hidden size {h} of 64")
+    admit(entry, gp.device, x=(x, Operand(HALF, layout=None)))
+    if x.ndim < 1 or x.shape[-1] != h:
+        refuse(entry, f"x has shape {tuple(x.shape)}, the MLP takes {h} features")
+    for name, (a, b, rows_in, rows_out) in {"gate": (ag, bg, h, n), "up": (au, bu, h, n),
+                                            "down": (ad, bd, n, h)}.items():
+        admit(entry, x.device, **{f"{name}_lora_a": (a, Operand(torch.float16, torch.float32, ndim=2, layout=None)),
+                                  f"{name}_lora_b": (b, Operand(torch.float16, torch.float32, ndim=2, layout=None))})
+        if a.shape[1] != rows_in or b.shape[0] != rows_out or b.shape[1] != a.shape[0]:
+            refuse(entry, f"{name} LoRA factors {tuple(a.shape)} / {tuple(b.shape)} do not fit")
+        if _padded_rank(a.shape[0]) > 32:
+            refuse(entry, f"{name} adapter rank {a.shape[0]} above 32")
+    if _padded_rank(ag.shape[0]) != _padded_rank(au.shape[0]):
+        refuse(entry, "gate and up adapters must pad to the same rank")
+    with torch.cuda.device(x.device):
+        return _FusedMLP.apply(x, scaling, gp, gs, ag, bg, up_p, us, au, bu, dp, ds, ad, bd)

@@ -20,12 +20,14 @@ reference's preregistered gate: rtol = atol = 2e-3, relative L2 <= 1e-3).
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import torch
 from torch.autograd.function import once_differentiable
 
 from .. import _lib
-from .nf4 import _validate_state
+from .._spec import FLOATS, HALF, Operand, admit, refuse
+from .nf4 import nested_shape
 
 _SUPPORTED_RANKS = (16, 32, 64)
 
@@ -46,7 +48,7 @@ def _padded_rank(r):
     for cand in _SUPPORTED_RANKS:
         if r <= cand:
             return cand
-    raise ValueError("LoRA rank above 64 is not supported")
+    raise ValueError(f"LoRA rank {r} is above the largest supported rank {_SUPPORTED_RANKS[-1]}")
 
 
 def _aligned16(t):
@@ -80,21 +82,20 @@ def nf4_linear_raw(x2d, packed, state, *, transpose=False, bias=None, lora_a=Non
 
 
 def nf4_matmul(x, packed, state, *, transpose=False, bias=None, config=None):
-    """Direct entry with the reference's signature (solution/kernels/nf4_gemm.py:74-96):
-    X[.., K] . deq(W)^T (+bias) or, with transpose=True, dY[.., N] . deq(W).
-    ``config`` is accepted for signature compatibility and ignored (one kernel)."""
-    n, k = _validate_state(packed, state, torch.float16)
-    if (not isinstance(x, torch.Tensor) or x.device != packed.device
-            or x.dtype != torch.float16 or not x.is_contiguous() or x.ndim < 2
-            or x.shape[-1] != (n if transpose else k)):
-        raise ValueError("Expected contiguous CUDA fp16 X matching canonical nested NF4 weight")
-    width = k if transpose else n
-    if bias is not None and (transpose or not isinstance(bias, torch.Tensor)
-            or bias.device != x.device or bias.dtype != torch.float16
-            or bias.shape != (width,) or not bias.is_contiguous() or bias.requires_grad):
-        raise ValueError("Only frozen contiguous fp16 forward bias is supported")
+    """Reference signature (solution/kernels/nf4_gemm.py:74-96): X[.., K] . deq(W)^T
+    (+ bias), or with transpose=True dY[.., N] . deq(W), as one fused launch.
+    ``config`` (a Triton tile choice there) is accepted and has no effect."""
+    n, k = nested_shape(packed, state, entry="nf4_matmul")
+    width, depth = (k, n) if transpose else (n, k)
+    admit("nf4_matmul", packed.device, x=(x, Operand(HALF, ndim=tuple(range(2, 9)))))
+    if x.shape[-1] != depth:
+        refuse("nf4_matmul", f"x has {x.shape[-1]} features, the weight takes {depth}")
+    if bias is not None and transpose:
+        refuse("nf4_matmul", "a bias applies to the forward product only")
+    admit("nf4_matmul", x.device,
+          bias=(bias, Operand(HALF, ndim=1, frozen=True, exactly=width, optional=True)))
     with torch.cuda.device(x.device):
-        out = nf4_linear_raw(x.reshape(-1, x.shape[-1]), packed, state, transpose=transpose, bias=bias)
+        out = nf4_linear_raw(x.reshape(-1, depth), packed, state, transpose=transpose, bias=bias)
     return out.reshape(*x.shape[:-1], width)
 
 
@@ -126,6 +127,31 @@ class _LoRAFactors:
                   self.b16.data_ptr(), self.bt16.data_ptr(), _lib.stream_of(dev))
 
 
+# Eager calls reuse the fp16 factor copies while the LoRA parameters are unchanged
+# (same storage, same in-place version counter): with several micro-batches per
+# optimizer step, or a layer called more than once, sb_lora_prepare runs once per
+# weight update.  Inside a CUDA-graph capture the conversion is always part of the
+# graph, because a replay has to see the parameters of its own time.
+_FACTOR_CACHE = {}
+
+
+def _factors(lora_a, lora_b):
+    if torch.cuda.is_current_stream_capturing():
+        return _LoRAFactors(lora_a, lora_b)
+    key = (id(lora_a), id(lora_b))
+    stamp = (lora_a.data_ptr(), lora_a._version, lora_a.dtype, tuple(lora_a.shape),
+             lora_b.data_ptr(), lora_b._version, lora_b.dtype, tuple(lora_b.shape),
+             torch.cuda.current_stream(lora_a.device).cuda_stream)
+    hit = _FACTOR_CACHE.get(key)
+    if hit is not None and hit[0] == stamp and hit[1]() is lora_a and hit[2]() is lora_b:
+        return hit[3]
+    f = _LoRAFactors(lora_a, lora_b)
+    if len(_FACTOR_CACHE) > 4096:
+        _FACTOR_CACHE.clear()
+    _FACTOR_CACHE[key] = (stamp, weakref.ref(lora_a), weakref.ref(lora_b), f)
+    return f
+
+
 def _project(x2d, w16, rp, scale_rows, want_rows, scale_t, want_t):
     """rows = fp16(scale_rows * X.W^T) [m, rp]; t = fp16(scale_t * X.W^T)^T [rp, m16]."""
     m, k = x2d.shape
@@ -152,24 +178,36 @@ def _reduce(pt, q2d, rp, scale, transpose, out_dtype):
 
 
 class _NF4LoRALinear(torch.autograd.Function):
+    """Y = X.deq(W)^T + s (D.A^T).B^T (+ bias) with D = X, or D = the caller's
+    dropped LoRA input (a separate differentiable input: the LoRA branch of a
+    PEFT layer in training sees dropout(X), the base projection sees X)."""
+
     @staticmethod
-    def forward(ctx, x, packed, state, lora_a, lora_b, scaling, bias):
+    def forward(ctx, x, packed, state, lora_a, lora_b, scaling, bias, lora_input):
         n, k = state.shape
         x2d = x.reshape(-1, k)
         if not x2d.is_contiguous():
             x2d = x2d.contiguous()
         has_lora = lora_a is not None
+        separate = lora_input is not None
         f = zt = None
         if has_lora:
-            f = _LoRAFactors(lora_a, lora_b)
-            zs, zt = _project(x2d, f.a16, f.rp, scaling, True, 1.0, True)
+            f = _factors(lora_a, lora_b)
+            d2d = x2d
+            if separate:
+                d2d = lora_input.reshape(-1, k).to(torch.float16).contiguous()
+            zs, zt = _project(d2d, f.a16, f.rp, scaling, True, 1.0, True)
             y = nf4_linear_raw(x2d, packed, state, bias=bias, lora_a=zs, lora_b=f.b16)
             ctx.a_dtype, ctx.b_dtype = lora_a.dtype, lora_b.dtype
-            ctx.save_for_backward(x2d, packed, zt, f.at16, f.bt16)
+            if separate:
+                ctx.d_dtype, ctx.d_shape = lora_input.dtype, lora_input.shape
+                ctx.save_for_backward(d2d, packed, zt, f.at16, f.bt16, f.a16)
+            else:
+                ctx.save_for_backward(x2d, packed, zt, f.at16, f.bt16)
         else:
             y = nf4_linear_raw(x2d, packed, state, bias=bias)
             ctx.save_for_backward(x2d, packed)
-        ctx.state, ctx.scaling, ctx.has_lora = state, float(scaling), has_lora
+        ctx.state, ctx.scaling, ctx.has_lora, ctx.separate = state, float(scaling), has_lora, separate
         ctx.r = f.r if has_lora else 0
         ctx.x_shape = x.shape
         return y.reshape(*x.shape[:-1], n)
@@ -182,53 +220,75 @@ class _NF4LoRALinear(torch.autograd.Function):
         g = grad.reshape(-1, n)
         if g.dtype != torch.float16 or not g.is_contiguous():
             g = g.to(torch.float16).contiguous()
-        dx = da = db = None
+        dx = da = db = dd = None
+        need_x = ctx.needs_input_grad[0]
         if ctx.has_lora:
-            x2d, packed, zt, at16, bt16 = ctx.saved_tensors
+            if ctx.separate:
+                d2d, packed, zt, at16, bt16, a16 = ctx.saved_tensors
+            else:
+                d2d, packed, zt, at16, bt16 = ctx.saved_tensors
             rp, r, s = at16.shape[1], ctx.r, ctx.scaling
-            need_x, need_a, need_b = ctx.needs_input_grad[0], ctx.needs_input_grad[3], ctx.needs_input_grad[4]
-            u, ut = _project(g, bt16, rp, s, need_x, s, need_a)
+            need_a, need_b = ctx.needs_input_grad[3], ctx.needs_input_grad[4]
+            need_d = ctx.separate and ctx.needs_input_grad[7]
+            # u = s dY.B: the rank-r factor of the LoRA input gradient (and of dA).
+            u, ut = _project(g, bt16, rp, s, need_x or need_d, s, need_a)
             if need_x:
-                dx = nf4_linear_raw(g, packed, state, transpose=True, lora_a=u, lora_b=at16)
+                if ctx.separate:
+                    dx = nf4_linear_raw(g, packed, state, transpose=True)
+                else:
+                    dx = nf4_linear_raw(g, packed, state, transpose=True, lora_a=u, lora_b=at16)
+            if need_d:
+                # d(loss)/dD = u . A, rank r: the expansion is one small fp16 product.
+                dd = torch.mm(u, a16).to(ctx.d_dtype).reshape(ctx.d_shape)
             if need_a:
-                da = _reduce(ut, x2d, rp, 1.0, False, ctx.a_dtype)[:r]
+                da = _reduce(ut, d2d, rp, 1.0, False, ctx.a_dtype)[:r]
             if need_b:
                 db = _reduce(zt, g, rp, s, True, ctx.b_dtype)[:, :r]
         else:
             x2d, packed = ctx.saved_tensors
-            if ctx.needs_input_grad[0]:
+            if need_x:
                 dx = nf4_linear_raw(g, packed, state, transpose=True)
         if dx is not None:
             dx = dx.reshape(ctx.x_shape)
-        return dx, None, None, da, db, None, None
+        return dx, None, None, da, db, None, None, dd
 
 
-def nf4_lora_linear(x, packed, state, lora_a=None, lora_b=None, scaling=1.0, bias=None):
+def nf4_lora_linear(x, packed, state, lora_a=None, lora_b=None, scaling=1.0, bias=None,
+                    lora_input=None):
     """Differentiable fused QLoRA projection (the north-star hot path).
 
     x: fp16 [..., K] CUDA; packed/state: nested NF4 weight W[N, K];
     lora_a: [r, K] (lora_A.weight), lora_b: [N, r] (lora_B.weight), trainable;
-    bias: optional frozen fp16 [N].  Returns fp16 [..., N].
+    bias: optional frozen fp16 [N]; lora_input: optional tensor of x's shape
+    (fp16 or fp32) that the LoRA branch reads instead of x -- a PEFT layer's
+    dropout(x) in training, whose gradient flows back through that dropout.
+    Returns fp16 [..., N].
     """
-    n, k = _validate_state(packed, state, torch.float16)
-    if (not isinstance(x, torch.Tensor) or x.device != packed.device or x.dtype != torch.float16
-            or x.ndim < 1 or x.shape[-1] != k):
-        raise ValueError("Expected CUDA fp16 X[..., K] matching the NF4 weight")
+    entry = "nf4_lora_linear"
+    n, k = nested_shape(packed, state, entry=entry)
+    admit(entry, packed.device, x=(x, Operand(HALF, layout=None)))
+    if x.ndim < 1 or x.shape[-1] != k:
+        refuse(entry, f"x has shape {tuple(x.shape)}, the weight takes {k} features")
     if (lora_a is None) != (lora_b is None):
-        raise ValueError("lora_a and lora_b must be given together")
+        refuse(entry, "lora_a and lora_b come together or not at all")
     if lora_a is not None:
-        if (lora_a.ndim != 2 or lora_b.ndim != 2 or lora_a.shape[1] != k or lora_b.shape[0] != n
-                or lora_a.shape[0] != lora_b.shape[1] or lora_a.device != x.device
-                or lora_b.device != x.device):
-            raise ValueError("Expected lora_a[r, K] and lora_b[N, r] on the input's device")
-        if lora_a.dtype not in (torch.float16, torch.float32) or lora_b.dtype not in (torch.float16, torch.float32):
-            raise ValueError("LoRA weights must be fp16 or fp32")
+        admit(entry, x.device, lora_a=(lora_a, Operand(*FLOATS, ndim=2, layout=None)),
+              lora_b=(lora_b, Operand(*FLOATS, ndim=2, layout=None)))
+        r = lora_a.shape[0]
+        if lora_a.shape[1] != k or tuple(lora_b.shape) != (n, r):
+            refuse(entry, f"LoRA factors {tuple(lora_a.shape)} / {tuple(lora_b.shape)} do not "
+                          f"fit a [{n}, {k}] weight")
         if k % 32 or n % 32:
-            raise ValueError("The fused LoRA path needs K and N multiples of 32")
-        _padded_rank(lora_a.shape[0])
-    if bias is not None and (bias.dtype != torch.float16 or bias.shape != (n,) or bias.requires_grad
-                             or bias.device != x.device):
-        raise ValueError("Only frozen fp16 bias[N] is supported")
+            refuse(entry, f"the fused LoRA step needs both weight sides divisible by 32, got {(n, k)}")
+        _padded_rank(r)
+    admit(entry, x.device, bias=(bias, Operand(HALF, ndim=1, frozen=True, exactly=n, layout=None,
+                                                optional=True)))
+    if lora_input is not None:
+        if lora_a is None:
+            refuse(entry, "lora_input without LoRA factors")
+        admit(entry, x.device, lora_input=(lora_input, Operand(*FLOATS, layout=None)))
+        if lora_input.shape != x.shape:
+            refuse(entry, f"lora_input has shape {tuple(lora_input.shape)}, x {tuple(x.shape)}")
     with torch.cuda.device(x.device):
         return _NF4LoRALinear.apply(x, packed, state, lora_a, lora_b, scaling,
-                                    None if bias is None else bias.contiguous())
+                                    None if bias is None else bias.contiguous(), lora_input)

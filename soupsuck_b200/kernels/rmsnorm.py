@@ -1,43 +1,47 @@
-"""Qwen2 RMSNorm with explicit cast order and an optional weight gradient.
+"""Qwen2 RMSNorm with the reference's cast order (reference API:
+solution/kernels/rmsnorm.py, ``rms_norm``).
 
-Mirror of solution/kernels/rmsnorm.py: r = rsqrt(mean(x^2) + eps), a = x*r in
-fp32, q = cast(a, x.dtype), y = weight * q in promote(x, weight) (or fp16).
-Backward: u = cast(g * weight, x.dtype), dx = r * (u - a * mean(u * a));
-dweight = sum(g * q) (each product rounded to fp16 when the exact output is
-fp16), two-stage and atomic-free.  Kernels: sb_rmsnorm_fwd /
-sb_rmsnorm_input_grad / sb_rmsnorm_weight_grad.
+    rstd = 1 / sqrt(mean(x^2) + eps)      a = x * rstd (fp32)      q = cast(a, x.dtype)
+    y    = weight * q   in promote(x, weight), or fp16 when asked
+
+    backward:  u = cast(g * weight, x.dtype),  dx = rstd * (u - a * mean(u * a))
+               dweight = sum over rows of g * q (products rounded to fp16 when the
+               norm's exact output is fp16), reduced in a fixed order
+
+Kernels ``sb_rmsnorm_fwd`` / ``sb_rmsnorm_input_grad`` / ``sb_rmsnorm_weight_grad``
+(csrc/rowwise.cuh).  The input may be a 2-D view whose rows are strided; any
+other input must be contiguous.
 """
 
 from __future__ import annotations
 
 import math
-import numbers
 
 import torch
 from torch.autograd.function import once_differentiable
 
-from .. import _lib
-from .add_rmsnorm import _weight_grad
+from .._spec import FLOATS, HALF, Choice, Number, Operand, admit, refuse
+from . import _rownorm
 
 
-class _RMSNorm(torch.autograd.Function):
+def _matrix(t, rows, width):
+    return t if t.ndim == 2 else t.reshape(rows, width)
+
+
+class _Norm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, eps, out_dtype):
-        h = x.shape[-1]
+        width = x.shape[-1]
         rows = math.prod(x.shape[:-1])
-        ctx.exact_dtype = torch.promote_types(x.dtype, weight.dtype)
-        out = torch.empty(x.shape, device=x.device, dtype=out_dtype or ctx.exact_dtype)
+        norm_dtype = torch.promote_types(x.dtype, weight.dtype)
+        y = torch.empty(x.shape, device=x.device, dtype=out_dtype or norm_dtype)
         rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
         if rows:
-            matrix = x if x.ndim == 2 else x.view(rows, h)
-            _lib.call("sb_rmsnorm_fwd", matrix.data_ptr(), _lib.dtype_code(x.dtype), matrix.stride(0),
-                      weight.data_ptr(), _lib.dtype_code(weight.dtype), weight.stride(0),
-                      out.data_ptr(), _lib.dtype_code(out.dtype), rstd.data_ptr(), rows, h,
-                      float(eps), _lib.stream_of(x.device))
+            _rownorm.norm_forward(_matrix(x, rows, width), weight, eps, y, rstd)
         ctx.save_for_backward(x, weight, rstd)
-        ctx.rows = rows
+        ctx.half_products = norm_dtype == HALF
         ctx.set_materialize_grads(False)
-        return out
+        return y
 
     @staticmethod
     @once_differentiable
@@ -45,41 +49,29 @@ class _RMSNorm(torch.autograd.Function):
         if grad is None:
             return None, None, None, None
         x, weight, rstd = ctx.saved_tensors
-        h, rows = x.shape[-1], ctx.rows
+        width = x.shape[-1]
+        rows = rstd.numel()
+        x2d, g2d = _matrix(x, rows, width), grad.reshape(rows, width)
         dx = dw = None
-        matrix = x if x.ndim == 2 else x.view(rows, h)
-        gmatrix = grad.reshape(rows, h)
         if ctx.needs_input_grad[0]:
             dx = torch.empty(x.shape, device=x.device, dtype=x.dtype)
             if rows:
-                _lib.call("sb_rmsnorm_input_grad", matrix.data_ptr(), _lib.dtype_code(x.dtype),
-                          matrix.stride(0), weight.data_ptr(), _lib.dtype_code(weight.dtype),
-                          weight.stride(0), gmatrix.data_ptr(), _lib.dtype_code(gmatrix.dtype),
-                          gmatrix.stride(0), gmatrix.stride(1), rstd.data_ptr(), dx.data_ptr(),
-                          rows, h, _lib.stream_of(x.device))
+                _rownorm.norm_input_grad(x2d, weight, g2d, rstd, dx)
         if ctx.needs_input_grad[1]:
-            if rows:
-                dw = _weight_grad(matrix, gmatrix, rstd, weight, ctx.exact_dtype == torch.float16)
-            else:
-                dw = torch.zeros(weight.shape, device=weight.device, dtype=weight.dtype)
+            dw = _rownorm.weight_grad(x2d, g2d, rstd, weight, ctx.half_products)
         return dx, dw, None, None
 
 
 def rms_norm(x, weight, eps, out_dtype=None):
-    """Normalize the last contiguous dimension, preserving Qwen2 cast semantics."""
-    if x.ndim < 1 or x.shape[-1] == 0 or weight.ndim != 1 or weight.shape[0] != x.shape[-1]:
-        raise ValueError("Expected x[...,H] and weight[H] with positive H")
-    if not x.is_cuda or weight.device != x.device:
-        raise ValueError("x and weight must be on the same CUDA device")
-    if x.stride(-1) != 1:
-        raise ValueError("The last input dimension must be contiguous")
-    if not x.is_contiguous() and x.ndim != 2:
-        raise ValueError("Noncontiguous leading dimensions require a 2-D input")
-    if x.dtype not in (torch.float16, torch.float32) or weight.dtype not in (torch.float16, torch.float32):
-        raise ValueError("RMSNorm supports only fp16/fp32 input and weight")
-    if not isinstance(eps, numbers.Real) or not math.isfinite(eps) or eps < 0:
-        raise ValueError("eps must be a finite nonnegative scalar")
-    if out_dtype not in (None, torch.float16):
-        raise ValueError("out_dtype must be None or torch.float16")
+    """RMSNorm over the last dimension of CUDA fp16/fp32 ``x`` with weight [H]."""
+    entry = "rms_norm"
+    device = x.device if isinstance(x, torch.Tensor) else None
+    admit(entry, device, x=(x, Operand(*FLOATS, layout="rows")),
+          weight=(weight, Operand(*FLOATS, ndim=1, layout=None)),
+          eps=(eps, Number(minimum=0)), out_dtype=(out_dtype, Choice(None, HALF)))
+    if x.ndim == 0 or x.shape[-1] == 0 or weight.shape[0] != x.shape[-1]:
+        refuse(entry, f"x {tuple(x.shape)} and weight {tuple(weight.shape)} must be [..., H] and [H], H > 0")
+    if x.ndim != 2 and not x.is_contiguous():
+        refuse(entry, "strided rows are accepted for 2-D inputs only")
     with torch.cuda.device(x.device):
-        return _RMSNorm.apply(x, weight, eps, out_dtype)
+        return _Norm.apply(x, weight, eps, out_dtype)

@@ -10,9 +10,10 @@ scale/add epilogue.  Here the whole projection
 is ``nf4_lora_linear`` (one LoRA-factor kernel and one tcgen05 GEMM with the
 LoRA product in the same TMEM accumulator; the backward gives dX through the
 same GEMM and dA / dB through the rank-r reductions).  When LoRA dropout is
-active (training with p > 0) the LoRA input differs from the base input, so
-the base runs through the fused GEMM alone and the LoRA branch keeps the
-reference's order (dropout on fp32 input, fp16 GEMMs, rounded epilogue).
+active (training with p > 0) the dropout runs first, on the reference's fp32
+LoRA input (so the RNG stream is the reference's), and the same fused GEMM
+takes the dropped activation for the LoRA factors and X for the NF4 base; the
+backward adds the LoRA branch's input gradient through that dropout.
 
 Numerics: the reference rounds the base result to fp16 and adds the fp16
 rounded LoRA term in fp32; the fused kernel accumulates both in fp32 and rounds
@@ -48,14 +49,14 @@ def _nf4_base(layer):
     bias = getattr(base, "bias", None)
     if bias is not None and (bias.requires_grad or bias.dtype != torch.float16):
         return None
-    from .kernels.nf4 import _validate_state
+    from .kernels.nf4 import nested_shape
 
     packed = weight.data if weight.is_contiguous() else None
     if packed is None:
         return None
     packed = packed.reshape(-1, 1)
     try:
-        n, k = _validate_state(packed, state, torch.float16)
+        n, k = nested_shape(packed, state, entry="Linear4bit")
     except ValueError:
         return None
     return packed, state, bias, n, k
@@ -116,18 +117,18 @@ def _patch_class(cls, variant_kwarg_keys):
 
         x16 = x if x.dtype == torch.float16 else x.to(torch.float16)
         active_dropout = (type(dropout) is torch.nn.Dropout and dropout.p > 0 and dropout.training)
-        autocast = torch.is_autocast_enabled("cuda")
-        if not active_dropout:
-            y = nf4_lora_linear(x16, packed, state, a.weight, b.weight, scaling, bias=bias)
-        else:
-            from .kernels.lora_epilogue import lora_epilogue
-
-            y = nf4_lora_linear(x16, packed, state, bias=bias)
+        dropped = None
+        if active_dropout:
+            # The dropout mask is drawn exactly as the reference's LoRA branch draws
+            # it (same input dtype, same point in the RNG stream); the fused GEMM
+            # then feeds the dropped activation to the LoRA factors and the raw
+            # input to the NF4 base in one accumulator.
             lora_input = x.float() if x.dtype == torch.float16 else x
-            if not autocast:
+            if not torch.is_autocast_enabled("cuda"):
                 lora_input = lora_input.to(a.weight.dtype)
-            lora_out = b(a(dropout(lora_input)))
-            return lora_epilogue(y.to(x.dtype), lora_out, scaling, cast_to_result=not autocast)
+            dropped = dropout(lora_input)
+        y = nf4_lora_linear(x16, packed, state, a.weight, b.weight, scaling, bias=bias,
+                            lora_input=dropped)
         return y.to(x.dtype)
 
     setattr(forward, _MARKER, original)

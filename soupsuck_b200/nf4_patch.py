@@ -1,24 +1,28 @@
-"""Route bitsandbytes 0.50.2's NF4 paths through the sm_100a kernels.
+"""bitsandbytes 0.50.2 NF4 entry points redirected to the sm_100a kernels.
 
-Mirror of the reference's solution/nf4_patch.py:43-125 (same three patched
-symbols, same marker attribute, same fallback rules) plus the matmul patch of
-solution/kernels/nf4_gemm.py:121-154, which here is on by default because the
-fused tcgen05 GEMM is the hot path (SOUP_EXP_NF4_GEMM=0 turns it off):
+Four library functions are replaced by wrappers that first try the library
+here and otherwise call the function they replaced (kept on the wrapper under
+the contract's marker attribute, ``_solution_fused_original``):
 
-* ``bitsandbytes.functional.dequantize_4bit`` - canonical nested fp16 NF4
-  states decode with ``sb_nf4_dequant_nested`` (into ``out`` when given);
-* ``bitsandbytes.backends.cuda.ops._dequantize_4bit_impl`` - inside a nested
-  ``_dequant_linear_fallback`` scope, decodes with ``sb_nf4_dequant_flat``;
-* ``..._dequant_linear_fallback`` - only marks that scope;
-* ``bitsandbytes.matmul_4bit`` - fp16 X against a canonical nested NF4 weight
-  runs the fused dequant-GEMM forward and dX (``sb_nf4_linear_fwd/dx``).
+  bitsandbytes.functional.dequantize_4bit          nested fp16 NF4 -> sb_nf4_dequant_nested
+  bitsandbytes.backends.cuda.ops._dequant_linear_fallback
+                                                    records whether its fp32 scales were
+                                                    rebuilt from a nested state
+  bitsandbytes.backends.cuda.ops._dequantize_4bit_impl
+                                                    inside such a call -> sb_nf4_dequant_flat
+  bitsandbytes.matmul_4bit                          fp16 X . NF4 W^T as the fused tcgen05
+                                                    GEMM (forward and dX); SOUP_EXP_NF4_GEMM=0
+                                                    keeps bitsandbytes' own
 
-Every unsupported input takes the saved original; only ``ValueError`` from
-validation is treated as "unsupported" and nothing raised by a kernel launch
-is swallowed.  Imports of torch and of the kernels are lazy.
+Reference behaviour kept (solution/nf4_patch.py:43-125, solution/kernels/nf4_gemm.py:121-154):
+only canonical nested fp16 NF4/block64 states are taken, anything the argument
+contracts refuse (a ValueError) runs the replaced function, and an error from
+a kernel launch propagates.  The nested-scales flag travels in a ContextVar,
+because only the linear fallback knows where its scales came from while the
+flat decoder it calls cannot tell.  Nothing here imports torch or the kernels
+until a wrapper runs.
 """
 
-from contextlib import contextmanager
 from contextvars import ContextVar
 from functools import wraps
 import importlib
@@ -28,143 +32,148 @@ from types import ModuleType
 from .utils import enabled
 
 _MARKER = "_solution_fused_original"
-_NESTED_BACKEND = ContextVar("soupsuck_b200_nf4_nested_backend", default=False)
+_PINNED_VERSION = "0.50.2"
+# True only while bitsandbytes' linear fallback that rebuilt fp32 scales from a
+# nested state is on the stack.
+_NESTED_BACKEND = ContextVar("soupsuck_b200_nested_scales", default=False)
 
 
-@contextmanager
-def _nested_backend_scope(nested):
-    token = _NESTED_BACKEND.set(nested)
+def _with_nested_flag(value, fn, *args, **kwargs):
+    token = _NESTED_BACKEND.set(value)
     try:
-        yield
+        return fn(*args, **kwargs)
     finally:
         _NESTED_BACKEND.reset(token)
 
 
-def _gemm_enabled():
-    return os.environ.get("SOUP_EXP_NF4_GEMM", "1") != "0"
+def _redirect(owner, attr, make):
+    """Install ``make(original)`` as ``owner.attr`` unless a wrapper is already there."""
+    original = getattr(owner, attr)
+    if hasattr(original, _MARKER):
+        return
+    wrapper = wraps(original)(make(original))
+    setattr(wrapper, _MARKER, original)
+    setattr(owner, attr, wrapper)
 
 
-def _make_dequantize(original_f):
-    @wraps(original_f)
-    def dequantize(A, quant_state=None, absmax=None, out=None, blocksize=None, quant_type="fp4"):
-        import torch
+def _cuda_tensor(value):
+    import torch
+    return isinstance(value, torch.Tensor) and value.is_cuda
 
-        arguments = dict(quant_state=quant_state, absmax=absmax, out=out,
-                         blocksize=blocksize, quant_type=quant_type)
 
-        def fallback():
-            with _nested_backend_scope(False):
-                return original_f(A, **arguments)
+# ------------------------------------------------------------------ the four routes
+def _functional_route(original):
+    def dequantize_4bit(A, quant_state=None, absmax=None, out=None, blocksize=None, quant_type="fp4"):
+        def library():
+            # bitsandbytes' own decode reaches _dequantize_4bit_impl too; that
+            # call must not be mistaken for the nested linear fallback.
+            return _with_nested_flag(False, original, A, quant_state=quant_state, absmax=absmax,
+                                     out=out, blocksize=blocksize, quant_type=quant_type)
 
-        if not enabled() or not isinstance(A, torch.Tensor) or not A.is_cuda:
-            return fallback()
-        from .kernels.nf4 import _validate_state, dequantize_nf4
-
+        if not enabled() or not _cuda_tensor(A):
+            return library()
+        from .kernels.nf4 import check_out, dequantize_nf4, nested_shape
         try:
-            shape = _validate_state(A, quant_state, torch.float16)
+            n, k = nested_shape(A, quant_state)
+            check_out(out, n, k, A.device)
         except ValueError:
-            return fallback()
-        if out is not None and (not isinstance(out, torch.Tensor) or tuple(out.shape) != shape
-                                or out.dtype != torch.float16 or out.device != A.device
-                                or not out.is_contiguous() or out.requires_grad):
-            return fallback()
+            return library()
         return dequantize_nf4(A, quant_state, out=out)
 
-    setattr(dequantize, _MARKER, original_f)
-    return dequantize
+    return dequantize_4bit
 
 
-def _make_backend(original_backend):
-    @wraps(original_backend)
-    def dequantize_backend(A, absmax, blocksize, quant_type, dtype, out):
+def _backend_route(original):
+    def _dequantize_4bit_impl(A, absmax, blocksize, quant_type, dtype, out):
         import torch
 
-        if (not _NESTED_BACKEND.get() or not enabled() or blocksize != 64
-                or quant_type != "nf4" or dtype != torch.float16):
-            return original_backend(A, absmax, blocksize, quant_type, dtype, out)
-        from .kernels.nf4 import _dequantize_flat_into, _validate_flat
+        if (enabled() and _NESTED_BACKEND.get() and quant_type == "nf4" and blocksize == 64
+                and dtype == torch.float16):
+            from .kernels.nf4 import decode_flat_into, flat_fault
+            if flat_fault(A, absmax, out) is None:
+                decode_flat_into(A, absmax, out)
+                return None  # bitsandbytes' helper fills `out` and returns nothing
+        return original(A, absmax, blocksize, quant_type, dtype, out)
 
-        try:
-            _validate_flat(A, absmax, out)
-        except ValueError:
-            return original_backend(A, absmax, blocksize, quant_type, dtype, out)
-        _dequantize_flat_into(A, absmax, out)
-        return None  # the original helper writes ``out`` and returns None
-
-    setattr(dequantize_backend, _MARKER, original_backend)
-    return dequantize_backend
+    return _dequantize_4bit_impl
 
 
-def _make_linear_fallback(original_linear):
-    @wraps(original_linear)
-    def linear_fallback(A, B, shapeB, absmax, blocksize, quant_type, bias=None,
-                        absmax_8bit=None, absmax_code=None, absmax_offset=None):
-        with _nested_backend_scope(absmax_8bit is not None):
-            return original_linear(A, B, shapeB, absmax, blocksize, quant_type, bias=bias,
-                                   absmax_8bit=absmax_8bit, absmax_code=absmax_code,
-                                   absmax_offset=absmax_offset)
+def _linear_fallback_route(original):
+    def _dequant_linear_fallback(A, B, shapeB, absmax, blocksize, quant_type, bias=None,
+                                 absmax_8bit=None, absmax_code=None, absmax_offset=None):
+        # absmax_8bit is present exactly when the fp32 scales were rebuilt from
+        # a nested state (the only case the flat route accepts).
+        return _with_nested_flag(absmax_8bit is not None, original, A, B, shapeB, absmax,
+                                 blocksize, quant_type, bias=bias, absmax_8bit=absmax_8bit,
+                                 absmax_code=absmax_code, absmax_offset=absmax_offset)
 
-    setattr(linear_fallback, _MARKER, original_linear)
-    return linear_fallback
+    return _dequant_linear_fallback
+
+
+def _matmul_fault(A, B, quant_state, out, bias):
+    """None when matmul_4bit can run as the fused GEMM, else why not."""
+    import torch
+
+    from ._spec import HALF, Operand, admit
+    from .kernels.nf4 import nested_shape
+
+    if out is not None:
+        return "an out= buffer was given"
+    try:
+        admit("matmul_4bit", None, A=(A, Operand(HALF, ndim=None, layout=None)),
+              B=(B, Operand(layout=None, frozen=True)))
+        if A.ndim < 2:
+            return "A is not a batch of rows"
+        packed = (B if B.is_contiguous() else B.contiguous()).reshape(-1, 1)
+        n, k = nested_shape(packed, quant_state, entry="matmul_4bit")
+        if A.shape[-1] != k:
+            return f"A has {A.shape[-1]} features, the weight {k}"
+        admit("matmul_4bit", A.device,
+              bias=(bias, Operand(HALF, ndim=1, frozen=True, exactly=n, optional=True)))
+        if torch.cuda.get_device_capability(A.device)[0] != 10:
+            return "not an sm_100 device"
+    except ValueError as err:
+        return str(err)
+    return None
 
 
 def make_matmul_4bit(original):
-    """``bitsandbytes.matmul_4bit(A, B, quant_state, out=None, bias=None)`` replacement.
+    """Wrapper for ``bitsandbytes.matmul_4bit(A, B, quant_state, out=None, bias=None)``.
 
-    bnb's Linear4bit passes ``B = weight.t()`` (a [1, nk/2] view of the packed
-    bytes); the weight is frozen, so autograd needs only dX (and no dW).
-    """
-    @wraps(original)
-    def matmul(A, B, quant_state, out=None, bias=None):
-        import torch
+    ``Linear4bit`` passes B = weight.t(), a [1, n*k/2] view of the packed codes;
+    the weight is frozen, so the autograd graph needs dX only."""
+    def matmul_4bit(A, B, quant_state, out=None, bias=None):
+        if (enabled() and os.environ.get("SOUP_EXP_NF4_GEMM", "1") != "0"
+                and _cuda_tensor(A) and _matmul_fault(A, B, quant_state, out, bias) is None):
+            from .kernels.nf4_gemm import nf4_lora_linear
+            packed = (B if B.is_contiguous() else B.contiguous()).reshape(-1, 1)
+            return nf4_lora_linear(A, packed, quant_state, bias=bias)
+        return original(A, B, quant_state, out=out, bias=bias)
 
-        shape = getattr(quant_state, "shape", ())
-        if (not enabled() or not _gemm_enabled() or len(shape) != 2
-                or not isinstance(A, torch.Tensor) or not A.is_cuda or A.dtype != torch.float16
-                or A.ndim < 2 or A.shape[-1] != shape[1] or out is not None
-                or not isinstance(B, torch.Tensor) or B.requires_grad
-                or (bias is not None and (not isinstance(bias, torch.Tensor) or bias.requires_grad
-                                          or bias.dtype != torch.float16 or bias.device != A.device
-                                          or tuple(bias.shape) != (shape[0],)))):
-            return original(A, B, quant_state, out=out, bias=bias)
-        from .kernels.nf4 import _validate_state
-        from .kernels.nf4_gemm import nf4_lora_linear
-        from .utils import supported_tensor
-
-        if not supported_tensor(A.contiguous() if not A.is_contiguous() else A):
-            return original(A, B, quant_state, out=out, bias=bias)
-        packed = B.reshape(-1, 1) if B.is_contiguous() else B.contiguous().reshape(-1, 1)
-        try:
-            _validate_state(packed, quant_state, torch.float16)
-        except ValueError:
-            return original(A, B, quant_state, out=out, bias=bias)
-        return nf4_lora_linear(A, packed, quant_state, bias=bias)
-
-    setattr(matmul, _MARKER, original)
-    return matmul
+    out = wraps(original)(matmul_4bit)
+    setattr(out, _MARKER, original)
+    return out
 
 
 def patch_bnb_dequant():
-    """Idempotently patch bitsandbytes 0.50.2; return whether it was patched."""
+    """Install the routes on bitsandbytes 0.50.2 (idempotent); False for any other version."""
     try:
         bnb = importlib.import_module("bitsandbytes")
         functional = importlib.import_module("bitsandbytes.functional")
         backend = importlib.import_module("bitsandbytes.backends.cuda.ops")
     except (ImportError, AttributeError):
         return False
-    if (not all(isinstance(m, ModuleType) for m in (bnb, functional, backend))
-            or getattr(bnb, "__version__", None) != "0.50.2"
-            or not callable(getattr(functional, "dequantize_4bit", None))
-            or not callable(getattr(backend, "_dequantize_4bit_impl", None))
-            or not callable(getattr(backend, "_dequant_linear_fallback", None))):
+    if not all(isinstance(m, ModuleType) for m in (bnb, functional, backend)):
         return False
-    if not hasattr(functional.dequantize_4bit, _MARKER):
-        functional.dequantize_4bit = _make_dequantize(functional.dequantize_4bit)
-    if not hasattr(backend._dequantize_4bit_impl, _MARKER):
-        backend._dequantize_4bit_impl = _make_backend(backend._dequantize_4bit_impl)
-    if not hasattr(backend._dequant_linear_fallback, _MARKER):
-        backend._dequant_linear_fallback = _make_linear_fallback(backend._dequant_linear_fallback)
-    original = getattr(bnb, "matmul_4bit", None)
-    if callable(original) and not hasattr(original, _MARKER):
-        bnb.matmul_4bit = make_matmul_4bit(original)
+    if getattr(bnb, "__version__", None) != _PINNED_VERSION:
+        return False
+    targets = ((functional, "dequantize_4bit", _functional_route),
+               (backend, "_dequantize_4bit_impl", _backend_route),
+               (backend, "_dequant_linear_fallback", _linear_fallback_route))
+    if not all(callable(getattr(owner, attr, None)) for owner, attr, _ in targets):
+        return False
+    for owner, attr, make in targets:
+        _redirect(owner, attr, make)
+    if callable(getattr(bnb, "matmul_4bit", None)) and not hasattr(bnb.matmul_4bit, _MARKER):
+        bnb.matmul_4bit = make_matmul_4bit(bnb.matmul_4bit)
     return True

@@ -43,18 +43,18 @@ def test_nested_bits_match_reference_goldens(entry):
 
 @pytest.mark.parametrize("entry", manifest()["nf4_flat"], ids=lambda e: str(e["n"]))
 def test_flat_signed_scales_and_unaligned_out(entry):
-    from soupsuck_b200.kernels.nf4 import _dequantize_flat_into
+    from soupsuck_b200.kernels.nf4 import decode_flat_into
     n = entry["n"]
     packed, _ = _fixture((1, n), 0.0)
     blocks = (n + 63) // 64
     scales = torch.linspace(-2, 2, blocks, device="cuda", dtype=torch.float32)
     expected = golden()[entry["key"]]
     out = torch.empty((1, n), device="cuda", dtype=torch.float16)
-    assert _dequantize_flat_into(packed, scales, out).data_ptr() == out.data_ptr()
+    assert decode_flat_into(packed, scales, out).data_ptr() == out.data_ptr()
     assert np.array_equal(bits16(out).reshape(-1), expected)
     guarded = torch.full((n + 2,), 123.0, device="cuda", dtype=torch.float16)
     view = guarded[1:n + 1].view(1, n)  # contiguous but not vector-store aligned
-    _dequantize_flat_into(packed, scales, view)
+    decode_flat_into(packed, scales, view)
     assert np.array_equal(bits16(view).reshape(-1), expected)
     assert guarded[0].item() == 123.0 and guarded[-1].item() == 123.0
 

@@ -144,22 +144,43 @@ def test_peft_linear4bit_forward_backward(fake_bnb_linear, fake_peft, m, n, k):
         assert rel < 2e-3, rel
 
 
-def test_peft_linear4bit_with_active_dropout_keeps_reference_branch(fake_bnb_linear, fake_peft):
+@pytest.mark.parametrize("x_dtype", [torch.float32, torch.float16])
+def test_peft_linear4bit_with_active_dropout_runs_fused_gemm(fake_bnb_linear, fake_peft, x_dtype):
+    """Training-mode LoRA dropout: same mask as the reference branch (same RNG
+    draw), the fused GEMM on the dropped LoRA input, gradients through the mask."""
     import soupsuck_b200.patch as patch
+    from soupsuck_b200 import _lib
 
     module, cls = fake_peft
     torch.manual_seed(5)
-    w = (torch.randn((512, 256), device="cuda") * 0.02).half()
+    m, n, k = 300, 1536, 512
+    w = (torch.randn((n, k), device="cuda") * 0.02).half()
     layer = cls(fake_bnb_linear(w), 16, 2.0, dropout=0.1).cuda().train()
+    with torch.no_grad():
+        layer.lora_A["default"].weight.uniform_(-1 / math.sqrt(k), 1 / math.sqrt(k))
+        layer.lora_B["default"].weight.normal_(0, 0.05)
     original = cls.forward
     patch._register_module(module.__name__, module)
-    x = torch.randn((64, 256), device="cuda", dtype=torch.float32)
+    x = torch.randn((m, k), device="cuda", dtype=x_dtype, requires_grad=True)
+    dy = torch.randn((m, n), device="cuda", dtype=x_dtype)
     torch.manual_seed(7)
+    before = _lib.launch_count()
     y = layer(x)
+    assert _lib.launch_count() > before
+    y.backward(dy)
+    got = (y.detach(), x.grad, layer.lora_A["default"].weight.grad, layer.lora_B["default"].weight.grad)
+    x.grad = None
+    layer.zero_grad()
     torch.manual_seed(7)
     y_ref = original(layer, x)
-    assert y.dtype == torch.float32
-    _gate(y, y_ref)
+    y_ref.backward(dy)
+    ref = (y_ref.detach(), x.grad, layer.lora_A["default"].weight.grad, layer.lora_B["default"].weight.grad)
+    assert got[0].dtype == ref[0].dtype == x_dtype
+    _gate(got[0], ref[0])
+    _gate(got[1], ref[1])
+    for g, r in zip(got[2:], ref[2:]):
+        rel = (g.double() - r.double()).norm() / r.double().norm()
+        assert rel < 2e-3, rel
 
 
 def test_matmul_4bit_patch_runs_fused_gemm(monkeypatch, fake_bnb_linear):
