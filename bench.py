@@ -5,10 +5,11 @@ projections (q 1536->1536, k/v 1536->256, o 1536->1536, gate/up 1536->8960,
 down 8960->1536), NF4/block64 + double-quant/block256 weights ~N(0, 0.02),
 LoRA r=16 alpha=32 on every projection, T=3300 packed fp16 tokens ~N(0, 1),
 fused residual add-RMSNorm (eps 1e-6, gamma ~N(1, 0.1)) before attention and
-before the MLP, forward plus backward (dX of every projection, LoRA dA/dB,
-norm gradients).  Attention and SwiGLU are outside the hot path: their outputs
-are synthetic inputs of o_proj / down_proj and their upstream gradients are
-synthetic too.  One step = that layer forward + backward on one micro-batch.
+before the MLP, the MLP itself as the fused gate/up -> SwiGLU -> down chain,
+forward plus backward (dX of every projection, LoRA dA/dB, norm gradients).
+Attention is outside the hot path: its output is a synthetic input of o_proj,
+and the upstream gradients of q, k, v and of the layer output are synthetic.
+One step = that layer forward + backward on one micro-batch.
 
 value     = algorithmic NF4-GEMM FLOPs of the step (fwd 2MNK+2MKr+2MrN,
             dX 2MNK+2MNr+2MrK per projection) / device time, whole job;
@@ -69,20 +70,29 @@ def nf4_weight_bytes(n, k):
 
 
 def pass_bytes(m):
-    """Algorithmic HBM bytes of the 14-launch GEMM pass: per launch the weight, the
-    activation read, the output written, the LoRA factor and the rank-r operand."""
+    """Algorithmic HBM bytes of one layer's GEMM pass (12 launches): per launch the
+    weight(s), the activation read, the output(s) written, the LoRA factors and the
+    rank-r operand.  q/k/v/o: forward and dX each.  MLP: gate/up forward (both
+    weights, X, gate|up and act written), down forward, down dX (dY and gate|up
+    read, dgate|dup written), two-weight dX (dgate|dup read, dX written)."""
+    r, h, n = RANK_R, HIDDEN, INTER
     total = 0
-    for _, n, k in PROJ:
-        one = nf4_weight_bytes(n, k) + 2 * m * k + 2 * m * n + 2 * RANK_R * (k + n) + 2 * m * RANK_R
+    for _, no, ki in PROJ[:4]:
+        one = nf4_weight_bytes(no, ki) + 2 * m * ki + 2 * m * no + 2 * r * (ki + no) + 2 * m * r
         total += 2 * one
+    wgu = 2 * nf4_weight_bytes(n, h)
+    total += wgu + 2 * m * h + 3 * 2 * m * n + 2 * (2 * r) * (h + 2 * n) + 2 * m * 2 * r      # gate/up + SwiGLU
+    total += nf4_weight_bytes(h, n) + 2 * m * n + 2 * m * h + 2 * r * (n + h) + 2 * m * r     # down
+    total += nf4_weight_bytes(h, n) + 2 * m * h + 2 * 2 * m * n + 2 * 2 * m * n + 2 * r * (n + h) + 2 * m * r  # down dX
+    total += wgu + 2 * 2 * m * n + 2 * m * h + 2 * (2 * r) * h + 2 * m * 2 * r                # gate/up dX
     return total
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one 14-launch GEMM
-# pass at T=3300, from a separate ncu capture of `bench.py --kernel-case
-# gemm_pass` (ncu cannot run inside the timed bench).  A static figure: it is
-# reported as such and describes the kernels of the capture it came from.
-PASS_TRAFFIC_NCU = {3300: 536506624}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one 12-launch GEMM
+# pass, from a separate ncu capture of `bench.py --kernel-case gemm_pass` (ncu
+# cannot run inside the timed bench).  A static figure: it is reported as such
+# and describes the kernels of the capture it came from.
+PASS_TRAFFIC_NCU = {}
 
 
 def static_pass_traffic(m):
@@ -192,36 +202,42 @@ def build_layer(torch, device, seed):
 
 
 def input_shapes(t):
-    return {"residual": (t, HIDDEN), "mlp_prev": (t, HIDDEN), "attn": (t, HIDDEN), "act": (t, INTER),
-            "g_q": (t, HIDDEN), "g_k": (t, KV), "g_v": (t, KV), "g_gate": (t, INTER),
-            "g_up": (t, INTER), "g_out": (t, HIDDEN)}
+    return {"residual": (t, HIDDEN), "mlp_prev": (t, HIDDEN), "attn": (t, HIDDEN),
+            "g_q": (t, HIDDEN), "g_k": (t, KV), "g_v": (t, KV), "g_out": (t, HIDDEN)}
+
+
+DIFF_INPUTS = ("residual", "attn", "mlp_prev")
 
 
 def layer_step(torch, layer, inp, streams=None):
     """Forward + backward of the hot path of one decoder layer (public API calls).
 
-    With ``streams`` (two side streams) the projections that do not depend on each
-    other run concurrently: o_proj and down_proj (their inputs are layer inputs)
-    on one side stream, k/v beside q and up beside gate on the other.  Autograd
-    runs every backward node on the stream of its forward, so the backward
-    overlaps the same way; all streams are joined before returning."""
-    from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear
+    add-RMSNorm, q/k/v, o, add-RMSNorm, then the MLP as the fused
+    gate/up(+SwiGLU) -> down chain (``nf4_swiglu_mlp``), residual add; backward
+    from synthetic upstream gradients of q, k, v and the layer output.  With
+    ``streams`` (two side streams) the projections that do not depend on each
+    other run concurrently: o_proj (its input is a layer input) on one side
+    stream, k/v beside q on the other.  Autograd runs every backward node on the
+    stream of its forward, so the backward overlaps the same way; all streams are
+    joined before returning."""
+    from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear, nf4_swiglu_mlp
     s = ALPHA / RANK_R
 
     def proj(name, x):
         packed, st, a, b = layer[name]
         return nf4_lora_linear(x, packed, st, a, b, s)
 
-    grads = [inp["g_q"], inp["g_k"], inp["g_v"], inp["g_gate"], inp["g_up"], inp["g_out"]]
+    def mlp(x):
+        return nf4_swiglu_mlp(x, layer["gate"], layer["up"], layer["down"], s)
+
+    grads = [inp["g_q"], inp["g_k"], inp["g_v"], inp["g_out"]]
     if streams is None:
         s1, y1 = add_rms_norm(inp["residual"], inp["mlp_prev"], layer["gamma_in"], EPS)
         q, k, v = proj("q", y1), proj("k", y1), proj("v", y1)
         o = proj("o", inp["attn"])
         s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
-        gate, up = proj("gate", y2), proj("up", y2)
-        down = proj("down", inp["act"])
-        out = s2 + down
-        torch.autograd.backward([q, k, v, gate, up, out], grads)
+        out = s2 + mlp(y2)
+        torch.autograd.backward([q, k, v, out], grads)
         return inp["residual"].grad
     main = torch.cuda.current_stream()
     sa, sb = streams
@@ -229,7 +245,6 @@ def layer_step(torch, layer, inp, streams=None):
     sb.wait_stream(main)
     with torch.cuda.stream(sb):
         o = proj("o", inp["attn"])
-        down = proj("down", inp["act"])
     s1, y1 = add_rms_norm(inp["residual"], inp["mlp_prev"], layer["gamma_in"], EPS)
     sa.wait_stream(main)
     with torch.cuda.stream(sa):
@@ -237,13 +252,9 @@ def layer_step(torch, layer, inp, streams=None):
     q = proj("q", y1)
     main.wait_stream(sb)
     s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
-    sa.wait_stream(main)
-    with torch.cuda.stream(sa):
-        up = proj("up", y2)
-    gate = proj("gate", y2)
-    out = s2 + down
+    out = s2 + mlp(y2)
     main.wait_stream(sa)
-    torch.autograd.backward([q, k, v, gate, up, out], grads)
+    torch.autograd.backward([q, k, v, out], grads)
     main.wait_stream(sa)
     main.wait_stream(sb)
     return inp["residual"].grad
@@ -310,40 +321,81 @@ def run_reference(args, torch):
 
 # ------------------------------------------------------------------ GPU timing helpers
 def gemm_roofline(torch, layer, device, t, passes=10, warm=3):
-    """Time the fused NF4 GEMM launches of one step (forward and dX of all seven
-    projections, LoRA fused) back to back with CUDA events on their stream."""
-    from soupsuck_b200.kernels.nf4_gemm import nf4_linear_raw
+    """Time the fused NF4 GEMM launches of one layer step back to back with CUDA
+    events on their stream: forward and dX of q, k, v, o (LoRA fused) and the
+    MLP's four launches -- gate/up with the SwiGLU epilogue, down, down dX with
+    the SwiGLU-derivative epilogue, and the two-weight gate/up dX (rank-32 LoRA
+    step for the gate/up pair).  Returns (FLOPs, seconds per pass, launches)."""
+    import ctypes
+
+    from soupsuck_b200 import _lib
+    from soupsuck_b200.kernels.nf4_gemm import _weight_struct, nf4_linear_raw
     calls = []
     flops = 0
-    for name, n, k in PROJ:
+    gen = torch.Generator(device=device).manual_seed(5)
+    rnd = lambda *shape: torch.randn(shape, device=device, dtype=torch.float16, generator=gen)
+    for name, n, k in PROJ[:4]:
         packed, st, a, b = layer[name]
-        x = torch.randn((t, k), device=device, dtype=torch.float16)
-        dy = torch.randn((t, n), device=device, dtype=torch.float16)
-        za = torch.randn((t, RANK_R), device=device, dtype=torch.float16)
+        x, dy, za = rnd(t, k), rnd(t, n), rnd(t, RANK_R)
         bt = b.detach().half().contiguous()
         at = a.detach().half().t().contiguous()
-        calls.append(lambda x=x, p=packed, s=st, za=za, bt=bt: nf4_linear_raw(x, p, s, lora_a=za, lora_b=bt))
-        calls.append(lambda dy=dy, p=packed, s=st, za=za, at=at: nf4_linear_raw(dy, p, s, transpose=True, lora_a=za, lora_b=at))
-        f, d = proj_flops(t, n, k, RANK_R)
-        flops += f + d
+        calls.append((f"{name} fwd", lambda x=x, p=packed, s=st, za=za, bt=bt:
+                      nf4_linear_raw(x, p, s, lora_a=za, lora_b=bt)))
+        calls.append((f"{name} dX", lambda dy=dy, p=packed, s=st, za=za, at=at:
+                      nf4_linear_raw(dy, p, s, transpose=True, lora_a=za, lora_b=at)))
+    stream = _lib.stream_of(device)
+    wg = _weight_struct(layer["gate"][0], layer["gate"][1])
+    wu = _weight_struct(layer["up"][0], layer["up"][1])
+    dp, ds, da_, db_ = layer["down"]
+    wd = _weight_struct(dp, ds)
+    x, dy = rnd(t, HIDDEN), rnd(t, HIDDEN)
+    z2, b_gu, u2, at_cat = rnd(t, 2 * RANK_R), rnd(2 * INTER, 2 * RANK_R), rnd(t, 2 * RANK_R), rnd(HIDDEN, 2 * RANK_R)
+    zd, bd16, ud, atd = rnd(t, RANK_R), db_.detach().half().contiguous(), rnd(t, RANK_R), da_.detach().half().t().contiguous()
+    gate_up, act, dgu = rnd(t, 2 * INTER), rnd(t, INTER), rnd(t, 2 * INTER)
+    dx = torch.empty((t, HIDDEN), device=device, dtype=torch.float16)
+    nbytes = _lib.query("sb_nf4_linear_dx2_workspace_bytes", t, INTER, HIDDEN)
+    ws = torch.empty(max(nbytes, 1), device=device, dtype=torch.uint8)
+    calls.append(("gate/up fwd + SwiGLU", lambda: _lib.call("sb_nf4_mlp_gate_up_fwd", x.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
+                                   z2.data_ptr(), b_gu.data_ptr(), 2 * RANK_R, gate_up.data_ptr(), act.data_ptr(),
+                                   stream)))
+    calls.append(("down fwd", lambda: nf4_linear_raw(act, dp, ds, lora_a=zd, lora_b=bd16)))
+    calls.append(("down dX + SwiGLU'", lambda: _lib.call("sb_nf4_mlp_down_dx", dy.data_ptr(), t, ctypes.byref(wd), ud.data_ptr(),
+                                   atd.data_ptr(), RANK_R, gate_up.data_ptr(), dgu.data_ptr(), stream)))
+    calls.append(("gate/up dX (two weights)", lambda: _lib.call("sb_nf4_linear_dx2", dgu.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
+                                   u2.data_ptr(), at_cat.data_ptr(), 2 * RANK_R, dx.data_ptr(), ws.data_ptr(),
+                                   nbytes, stream)))
+    flops = step_flops(t)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for _ in range(warm):
-        for c in calls:
+        for _, c in calls:
             c()
     torch.cuda.synchronize()
-    stream = torch.cuda.current_stream(device)
+    cur = torch.cuda.current_stream(device)
     times = []
     for _ in range(passes):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for c in calls:
+        e0.record(cur)
+        for _, c in calls:
             c()
-        e1.record(stream)
+        e1.record(cur)
         e1.synchronize()
         times.append(e0.elapsed_time(e1) / 1000.0)
     sec = statistics.median(times)
-    return flops, sec, len(calls)
+    # Each launch alone (L2 flushed before it), for the per-kernel breakdown.
+    per_launch = {}
+    for label, c in calls:
+        samples = []
+        for _ in range(max(3, passes // 2)):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            c()
+            e1.record(cur)
+            e1.synchronize()
+            samples.append(e0.elapsed_time(e1) * 1000.0)
+        per_launch[label] = round(statistics.median(samples), 1)
+    return flops, sec, len(calls), per_launch
 
 
 def ce_benchmark(torch, device, steps, tokens=T_TOKENS, warm=2):
@@ -413,10 +465,10 @@ def kernel_case(args, torch):
         gen = torch.Generator(device=device).manual_seed(1000)
         inp = {name: torch.randn(shp, device=device, dtype=torch.float16, generator=gen)
                for name, shp in input_shapes(t).items()}
-        for name in ("residual", "attn", "act", "mlp_prev"):
+        for name in DIFF_INPUTS:
             inp[name].requires_grad_()
         for _ in range(args.warmup + args.steps):
-            for name in ("residual", "attn", "act", "mlp_prev"):
+            for name in DIFF_INPUTS:
                 inp[name].grad = None
             layer_step(torch, layer, inp)
     elif args.kernel_case == "ce":
@@ -573,13 +625,11 @@ def stack_lengths():
 
 def stack_step(torch, layers, x, delta, g_out, g_kv, side=None):
     """Forward + backward of the 28-layer projection stack on one packed batch.
-    Attention and the MLP activation are outside the hot path: o_proj reads q in
-    place of the attention output (same shape), down_proj reads silu(gate) * up
-    (torch elementwise).  With ``side`` (a stream) k/v run beside q and up beside
-    gate, forward and (autograd keeps each backward node on its forward's stream)
-    backward."""
-    import torch.nn.functional as F
-    from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear
+    Attention is outside the hot path: o_proj reads q in place of the attention
+    output (same shape).  The MLP is the fused gate/up -> SwiGLU -> down chain.
+    With ``side`` (a stream) k/v run beside q, forward and (autograd keeps each
+    backward node on its forward's stream) backward."""
+    from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear, nf4_swiglu_mlp
     s = ALPHA / RANK_R
 
     def proj(layer, name, inp):
@@ -604,20 +654,10 @@ def stack_step(torch, layers, x, delta, g_out, g_kv, side=None):
         q = proj(layer, "q", y1)
         o = proj(layer, "o", q)
         s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
-        if side is not None:
-            side.wait_stream(main)
-            with torch.cuda.stream(side):
-                up = proj(layer, "up", y2)
-            y2.record_stream(side)
-            gate = proj(layer, "gate", y2)
-            main.wait_stream(side)
-            up.record_stream(main)
-        else:
-            gate, up = proj(layer, "gate", y2), proj(layer, "up", y2)
-        down = proj(layer, "down", F.silu(gate) * up)
+        mlp = nf4_swiglu_mlp(y2, layer["gate"], layer["up"], layer["down"], s)
         outs += [k, v]
         grads += [g_kv, g_kv]
-        res, dlt = s2, down
+        res, dlt = s2, mlp
     outs.append(res + dlt)
     grads.append(g_out)
     if side is not None:
@@ -757,7 +797,7 @@ def run_stack(args, torch):
             "config": {"workload": "configs[2]: 28 layers x 7 NF4+LoRA(r=16) projections + 2 add-RMSNorm, fwd+bwd",
                        "batches": STACK_BATCHES, "tokens": tokens, "padded_rows": padded,
                        "bucket_rows": STACK_BUCKET, "cuda_graph": bool(graphs), "graphs": len(graphs),
-                       "streams": "k/v and up on a side stream" if kv_stream is not None else "one stream",
+                       "streams": "k/v on a side stream" if kv_stream is not None else "one stream",
                        "parallelism": f"dp{world}"},
             "clocks": clocks.summary(), "device_error": err}), flush=True)
     del graphs
@@ -823,13 +863,13 @@ def main():
     dev_in = {}
     for name, shp in shapes.items():
         dev_in[name] = torch.randn(shp, device=device, dtype=torch.float16, generator=g)
-    for name in ("residual", "attn", "act", "mlp_prev"):
+    for name in DIFF_INPUTS:
         dev_in[name].requires_grad_()
 
     def zero_grads():
         for p in params:
             p.grad = None
-        for name in ("residual", "attn", "act", "mlp_prev"):
+        for name in DIFF_INPUTS:
             dev_in[name].grad = None
 
     def allreduce_grads():
@@ -871,13 +911,13 @@ def main():
         torch.cuda.current_stream(device).wait_stream(side)
         torch.cuda.synchronize()
         second = {k: v.detach().clone() for k, v in dev_in.items()}
-        for name in ("residual", "attn", "act", "mlp_prev"):
+        for name in DIFF_INPUTS:
             second[name].requires_grad_()
         sets.append(second)
         for inputs in sets:
             for p in params:
                 p.grad = None
-            for name in ("residual", "attn", "act", "mlp_prev"):
+            for name in DIFF_INPUTS:
                 inputs[name].grad = None
             g_ = torch.cuda.CUDAGraph()
             before = _lib.launch_count()
@@ -1012,7 +1052,7 @@ def main():
         return 0
 
     peak_burst, peak_sust, hbm, peak_kind = measured_peaks()
-    gflops, gsec, glaunch = gemm_roofline(torch, layer, device, t)
+    gflops, gsec, glaunch, per_launch = gemm_roofline(torch, layer, device, t)
     achieved = gflops / gsec / 1e12
     ce = None if args.no_ce else ce_benchmark(torch, device, args.steps)
     cpu = None
@@ -1023,12 +1063,13 @@ def main():
         "warmup": args.warmup, "ms_per_step": 1000 * sec_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) NF4 weights)",
-        "config": {"workload": "configs[1]: Qwen2.5-1.5B layer, 7 NF4+LoRA(r=16) projections + 2 add-RMSNorm, fwd+bwd",
+        "config": {"workload": "configs[1]: Qwen2.5-1.5B layer, 7 NF4+LoRA(r=16) projections + 2 add-RMSNorm "
+                               "+ SwiGLU (fused MLP), fwd+bwd",
                    "tokens_per_gpu": t, "global_tokens": t * world,
                    "parallelism": f"dp{world}" + (" + LoRA-grad NCCL all-reduce" if world > 1 else ""),
                    "l2": "flushed (256 MiB write) before every timed step, outside the events",
                    "cuda_graph": used_graph,
-                   "streams": "o/down, k/v and up on two side streams" if streams else "one stream"},
+                   "streams": "o and k/v on two side streams" if streams else "one stream"},
         "pct_peak": 100.0 * value / (peak_burst * world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": 1000 * e2e_sec,
@@ -1040,9 +1081,10 @@ def main():
                      "traffic_source": "static ncu figure (DRAM bytes per pass of the 14 launches, "
                                        "captured separately from this run)",
                      "algorithmic_bytes": pass_bytes(t),
-                     "kernel": "pair_kernel<NF4> (cta_group::2) fwd+dX, LoRA fused",
+                     "kernel": "pair_kernel<NF4> (cta_group::2): q/k/v/o fwd+dX, MLP gate/up+SwiGLU, down, "
+                               "down dX+SwiGLU', gate/up two-weight dX; LoRA fused",
                      "peak_source": f"{peak_kind} bf16 dense burst (MEASURED_PEAKS.json)",
-                     "launches": glaunch, "ms_per_pass": 1000 * gsec},
+                     "launches": glaunch, "ms_per_pass": 1000 * gsec, "per_launch_us": per_launch},
         "clocks": clocks.summary(),
         "device_error": dev_err,
     }

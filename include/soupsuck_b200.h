@@ -266,6 +266,26 @@ int sb_nf4_linear_dx2(const uint16_t* dy2, int64_t m, const sb_nf4_weight* w1, c
                       const uint16_t* lora_a, const uint16_t* lora_b, int r, uint16_t* dx, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- Unpadding
+ * Right-padded batches packed to their real tokens (solution/unpad.py: mask rules
+ * :51-72, _batch_metadata :164-183, _indices_from_lengths :186-200, _pack :149-150,
+ * _scatter :153-161).  mask [batch, seq] with mask_dtype 0 int64, 1 int32, 2 uint8 /
+ * bool, 3 fp16, 4 fp32; labels [batch, seq] int64 or NULL.
+ * sb_unpad_metadata: cu_seqlens[0..batch] = exclusive prefix of the per-row real
+ *   lengths and cu_seqlens[batch + 1] = validity bits (1 a value other than 0/1,
+ *   2 a one after a zero, 4 a padded label other than ignore_index, 8 an empty
+ *   row); cu_seqlens holds batch + 2 int32.  workspace: sb_unpad_workspace_bytes(batch).
+ * sb_unpad_pack: packed[i] = x[b, i - cu[b]] for the `rows` real rows, rows of
+ *   row_bytes bytes.  sb_unpad_scatter: out[b, t] = packed[cu[b] + t] for t below
+ *   the row's length, zero bytes elsewhere.  Byte copies (16-byte when aligned). */
+size_t sb_unpad_workspace_bytes(int64_t batch);
+int sb_unpad_metadata(const void* mask, int mask_dtype, const int64_t* labels, int64_t ignore_index, int64_t batch,
+                      int64_t seq, int32_t* cu_seqlens, void* workspace, size_t workspace_bytes, void* stream);
+int sb_unpad_pack(const void* x, int64_t batch, int64_t seq, int64_t row_bytes, const int32_t* cu_seqlens,
+                  int64_t rows, void* packed, void* stream);
+int sb_unpad_scatter(const void* packed, int64_t batch, int64_t seq, int64_t row_bytes, const int32_t* cu_seqlens,
+                     void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -435,3 +435,49 @@ def swiglu_backward(gate, up, grad, gate_dtype=None, up_dtype=None):
     dg = ((da * u).astype(F32) * slope).astype(F32)
     du = (da * act).astype(F32)
     return dg.astype(gate_dtype or gate.dtype), du.astype(up_dtype or up.dtype)
+
+
+# --------------------------------------------------------------------------
+# Right-padding removal (solution/unpad.py:51-72, :149-200)
+# --------------------------------------------------------------------------
+
+def unpad_lengths(mask, labels=None, ignore_index: int = -100):
+    """Real-token count per row of a binary right-padded mask whose padded positions
+    carry ignore_index labels, or None when any rule fails (a value other than 0/1,
+    a one after a zero, a padded label, an empty row) -- _batch_metadata (:164-183)
+    followed by right_padding_lengths (:51-72)."""
+    mask = np.asarray(mask)
+    if mask.ndim != 2 or mask.shape[0] == 0 or mask.shape[1] == 0:
+        return None
+    real = mask == 1
+    if not ((mask == 0) | real).all():
+        return None
+    if labels is not None and not (real | (np.asarray(labels) == ignore_index)).all():
+        return None
+    lengths = real.sum(axis=1)
+    if (lengths == 0).any():
+        return None
+    prefix = np.arange(mask.shape[1])[None, :] < lengths[:, None]
+    if not np.array_equal(prefix, real):
+        return None
+    return tuple(int(x) for x in lengths)
+
+
+def unpad_indices(lengths, sequence: int):
+    """Row-major positions b*S + t of the real tokens (_indices_from_lengths :186-200)."""
+    return np.concatenate([b * sequence + np.arange(n) for b, n in enumerate(lengths)]).astype(np.int64)
+
+
+def unpad_pack(x, lengths):
+    """[B, S, ...] -> [T, ...] (the index_select of _pack :149-150)."""
+    x = np.asarray(x)
+    flat = x.reshape(x.shape[0] * x.shape[1], *x.shape[2:])
+    return flat[unpad_indices(lengths, x.shape[1])]
+
+
+def unpad_scatter(packed, lengths, sequence: int):
+    """[T, ...] -> zero-padded [B, S, ...] (the index_copy of _scatter :153-161)."""
+    packed = np.asarray(packed)
+    out = np.zeros((len(lengths) * sequence, *packed.shape[1:]), dtype=packed.dtype)
+    out[unpad_indices(lengths, sequence)] = packed
+    return out.reshape(len(lengths), sequence, *packed.shape[1:])

@@ -74,6 +74,10 @@ SIGNATURES = {
     "sb_nf4_linear_dx2_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sb_nf4_linear_dx2": (_I32, [_P, _I64, ctypes.POINTER(NF4Weight), ctypes.POINTER(NF4Weight), _P, _P, _I32,
                                  _P, _P, _SZ, _P]),
+    "sb_unpad_workspace_bytes": (_SZ, [_I64]),
+    "sb_unpad_metadata": (_I32, [_P, _I32, _P, _I64, _I64, _I64, _P, _P, _SZ, _P]),
+    "sb_unpad_pack": (_I32, [_P, _I64, _I64, _I64, _P, _I64, _P, _P]),
+    "sb_unpad_scatter": (_I32, [_P, _I64, _I64, _I64, _P, _P, _P]),
 }
 
 _lock = threading.Lock()

@@ -7,8 +7,11 @@
 //   p  = 1 / (1 + exp(-g))        a  = (g * p) * u
 //   dg = (da * u) * (p + (g p) (1 - p))        du = da * (g p)
 //
-// Each operation is rounded separately (explicit _rn intrinsics, no contraction);
-// exp is CUDA's expf.  Results are stored in fp16.
+// Each multiply and add is rounded separately (explicit _rn intrinsics, no
+// contraction).  The exponential and the reciprocal are the fast hardware forms
+// (__expf, __fdividef), the same approximation class as the reference's
+// tl.exp and fp32 division on the GPU; their few-ulp fp32 error is far below the
+// fp16 rounding of the results.
 #pragma once
 
 #include "common.cuh"
@@ -16,7 +19,7 @@
 namespace sb {
 namespace swiglu {
 
-__device__ __forceinline__ float sigmoid(float g) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))); }
+__device__ __forceinline__ float sigmoid(float g) { return __fdividef(1.0f, __fadd_rn(1.0f, __expf(-g))); }
 
 __device__ __forceinline__ float forward(float g, float u) {
   return __fmul_rn(__fmul_rn(g, sigmoid(g)), u);

@@ -118,6 +118,9 @@ def _pair_factors(ag, bg, au, bu):
 
 
 class _FusedMLP(torch.autograd.Function):
+    """Forward/backward of the fused MLP.  The gate/up adapters come as a pair or
+    not at all (r = 0 for the pair kernel), the down adapter independently."""
+
     @staticmethod
     def forward(ctx, x, scaling, g_packed, g_state, ag, bg, u_packed, u_state, au, bu, d_packed, d_state, ad, bd):
         n, h = g_state.shape
@@ -126,25 +129,34 @@ class _FusedMLP(torch.autograd.Function):
             x2d = x2d.contiguous()
         t = x2d.shape[0]
         dev = x.device
-        pf = _pair_factors(ag, bg, au, bu)
-        fd = _factors(ad, bd)
         s = float(scaling)
         stream = _lib.stream_of(dev)
-        z_rows, z_t = _project(x2d, pf.a_cat, 2 * pf.rp, s, True, 1.0, True)
+        pf = _pair_factors(ag, bg, au, bu) if ag is not None else None
+        fd = _factors(ad, bd) if ad is not None else None
+        z_rows = z_t = None
+        if pf is not None:
+            z_rows, z_t = _project(x2d, pf.a_cat, 2 * pf.rp, s, True, 1.0, True)
         gate_up = torch.empty((t, 2 * n), device=dev, dtype=HALF)
         act = torch.empty((t, n), device=dev, dtype=HALF)
         wg, wu = _weight_struct(g_packed, g_state), _weight_struct(u_packed, u_state)
         if t:
             _lib.call("sb_nf4_mlp_gate_up_fwd", x2d.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
-                      z_rows.data_ptr(), pf.b_gu.data_ptr(), 2 * pf.rp, gate_up.data_ptr(), act.data_ptr(),
-                      stream)
-        zd_rows, zd_t = _project(act, fd.a16, fd.rp, s, True, 1.0, True)
-        y = nf4_linear_raw(act, d_packed, d_state, lora_a=zd_rows, lora_b=fd.b16)
-        ctx.save_for_backward(x2d, gate_up, act, z_t, zd_t, pf.at_cat, pf.bt_bd, fd.at16, fd.bt16,
+                      _lib.ptr(z_rows), None if pf is None else pf.b_gu.data_ptr(),
+                      0 if pf is None else 2 * pf.rp, gate_up.data_ptr(), act.data_ptr(), stream)
+        zd_t = None
+        if fd is not None:
+            zd_rows, zd_t = _project(act, fd.a16, fd.rp, s, True, 1.0, True)
+            y = nf4_linear_raw(act, d_packed, d_state, lora_a=zd_rows, lora_b=fd.b16)
+        else:
+            y = nf4_linear_raw(act, d_packed, d_state)
+        ctx.save_for_backward(x2d, gate_up, act, z_t, zd_t,
+                              None if pf is None else pf.at_cat, None if pf is None else pf.bt_bd,
+                              None if fd is None else fd.at16, None if fd is None else fd.bt16,
                               g_packed, u_packed, d_packed)
         ctx.states = (g_state, u_state, d_state)
-        ctx.meta = (s, pf.rp, pf.r_gate, pf.r_up, fd.r, x.shape, ag.dtype, bg.dtype, au.dtype, bu.dtype,
-                    ad.dtype, bd.dtype)
+        dtypes = tuple(None if p is None else p.dtype for p in (ag, bg, au, bu, ad, bd))
+        ctx.meta = (s, None if pf is None else (pf.rp, pf.r_gate, pf.r_up),
+                    None if fd is None else fd.r, x.shape, dtypes)
         return y.reshape(*x.shape[:-1], d_state.shape[0])
 
     @staticmethod
@@ -152,7 +164,7 @@ class _FusedMLP(torch.autograd.Function):
     def backward(ctx, grad):
         (x2d, gate_up, act, z_t, zd_t, at_cat, bt_bd, at_d, bt_d, g_packed, u_packed, d_packed) = ctx.saved_tensors
         g_state, u_state, d_state = ctx.states
-        s, rp, r_gate, r_up, r_down, x_shape, ag_t, bg_t, au_t, bu_t, ad_t, bd_t = ctx.meta
+        s, pair, r_down, x_shape, (ag_t, bg_t, au_t, bu_t, ad_t, bd_t) = ctx.meta
         n, h = g_state.shape
         hd = d_state.shape[0]
         g = grad.reshape(-1, hd)
@@ -161,41 +173,54 @@ class _FusedMLP(torch.autograd.Function):
         t = g.shape[0]
         dev = g.device
         stream = _lib.stream_of(dev)
-        # down: rank-r factor of its input gradient, then dact -> (dgate, dup) in one launch
-        rpd = at_d.shape[1]
-        ud, ud_t = _project(g, bt_d, rpd, s, True, s, True)
+        # down: dact (with its LoRA term) -> (dgate, dup) in one launch
+        ud = ud_t = None
+        rpd = 0
+        if at_d is not None:
+            rpd = at_d.shape[1]
+            ud, ud_t = _project(g, bt_d, rpd, s, True, s, True)
         dgate_up = torch.empty((t, 2 * n), device=dev, dtype=HALF)
         wd = _weight_struct(d_packed, d_state)
         if t:
-            _lib.call("sb_nf4_mlp_down_dx", g.data_ptr(), t, ctypes.byref(wd), ud.data_ptr(), at_d.data_ptr(),
+            _lib.call("sb_nf4_mlp_down_dx", g.data_ptr(), t, ctypes.byref(wd), _lib.ptr(ud), _lib.ptr(at_d),
                       rpd, gate_up.data_ptr(), dgate_up.data_ptr(), stream)
-        d_ad = _reduce(ud_t, act, rpd, 1.0, False, ad_t)[:r_down]
-        d_bd = _reduce(zd_t, g, rpd, s, True, bd_t)[:, :r_down]
+        d_ad = d_bd = None
+        if at_d is not None:
+            d_ad = _reduce(ud_t, act, rpd, 1.0, False, ad_t)[:r_down]
+            d_bd = _reduce(zd_t, g, rpd, s, True, bd_t)[:, :r_down]
         # gate + up: one reduction over both weights, both LoRA terms in one rank-2rp step
-        u_cat, u_cat_t = _project(dgate_up, bt_bd, 2 * rp, s, True, s, True)
+        u_cat = u_cat_t = None
+        r2 = 0
+        if pair is not None:
+            rp = pair[0]
+            r2 = 2 * rp
+            u_cat, u_cat_t = _project(dgate_up, bt_bd, r2, s, True, s, True)
         dx = torch.empty((t, h), device=dev, dtype=HALF)
         wg, wu = _weight_struct(g_packed, g_state), _weight_struct(u_packed, u_state)
         if t:
             nbytes = _lib.query("sb_nf4_linear_dx2_workspace_bytes", t, n, h)
             scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
             _lib.call("sb_nf4_linear_dx2", dgate_up.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
-                      u_cat.data_ptr(), at_cat.data_ptr(), 2 * rp, dx.data_ptr(), scratch.data_ptr(), nbytes,
-                      stream)
-        d_acat = _reduce(u_cat_t, x2d, 2 * rp, 1.0, False, torch.float32)
-        d_bgu = _reduce(z_t, dgate_up, 2 * rp, s, True, torch.float32)
-        d_ag = d_acat[:r_gate].to(ag_t)
-        d_au = d_acat[rp:rp + r_up].to(au_t)
-        d_bg = d_bgu[:n, :r_gate].to(bg_t)
-        d_bu = d_bgu[n:, rp:rp + r_up].to(bu_t)
+                      _lib.ptr(u_cat), _lib.ptr(at_cat), r2, dx.data_ptr(), scratch.data_ptr(), nbytes, stream)
+        d_ag = d_bg = d_au = d_bu = None
+        if pair is not None:
+            rp, r_gate, r_up = pair
+            d_acat = _reduce(u_cat_t, x2d, r2, 1.0, False, torch.float32)
+            d_bgu = _reduce(z_t, dgate_up, r2, s, True, torch.float32)
+            d_ag = d_acat[:r_gate].to(ag_t)
+            d_au = d_acat[rp:rp + r_up].to(au_t)
+            d_bg = d_bgu[:n, :r_gate].to(bg_t)
+            d_bu = d_bgu[n:, rp:rp + r_up].to(bu_t)
         return (dx.reshape(x_shape), None, None, None, d_ag, d_bg, None, None, d_au, d_bu, None, None,
                 d_ad, d_bd)
 
 
 def nf4_swiglu_mlp(x, gate, up, down, scaling=1.0):
-    """Differentiable Qwen2 MLP ``down(SwiGLU(gate(x), up(x)))`` on NF4 weights with
-    LoRA on every projection.  x: fp16 [..., H] CUDA; gate / up / down: tuples
-    (packed, quant_state, lora_a [r, in], lora_b [out, r]) with gate/up [N, H] and
-    down [H, N]; N a multiple of 128, H and N multiples of 64; adapter ranks <= 32.
+    """Differentiable Qwen2 MLP ``down(SwiGLU(gate(x), up(x)))`` on NF4 weights.
+    x: fp16 [..., H] CUDA; gate / up / down: tuples (packed, quant_state, lora_a,
+    lora_b) with gate/up [N, H] and down [H, N] (N a multiple of 128, H of 64);
+    lora_a [r, in] / lora_b [out, r] are the adapter (r <= 32) or both None (a
+    frozen projection; gate and up have adapters together or neither).
     Returns fp16 [..., H]."""
     entry = "nf4_swiglu_mlp"
     (gp, gs, ag, bg), (up_p, us, au, bu), (dp, ds, ad, bd) = gate, up, down
@@ -207,15 +232,21 @@ def nf4_swiglu_mlp(x, gate, up, down, scaling=1.0):
     admit(entry, gp.device, x=(x, Operand(HALF, layout=None)))
     if x.ndim < 1 or x.shape[-1] != h:
         refuse(entry, f"x has shape {tuple(x.shape)}, the MLP takes {h} features")
+    if (ag is None) != (bg is None) or (au is None) != (bu is None) or (ad is None) != (bd is None):
+        refuse(entry, "each adapter needs both factors or none")
+    if (ag is None) != (au is None):
+        refuse(entry, "gate and up carry adapters together or not at all")
     for name, (a, b, rows_in, rows_out) in {"gate": (ag, bg, h, n), "up": (au, bu, h, n),
                                             "down": (ad, bd, n, h)}.items():
+        if a is None:
+            continue
         admit(entry, x.device, **{f"{name}_lora_a": (a, Operand(torch.float16, torch.float32, ndim=2, layout=None)),
                                   f"{name}_lora_b": (b, Operand(torch.float16, torch.float32, ndim=2, layout=None))})
         if a.shape[1] != rows_in or b.shape[0] != rows_out or b.shape[1] != a.shape[0]:
             refuse(entry, f"{name} LoRA factors {tuple(a.shape)} / {tuple(b.shape)} do not fit")
         if _padded_rank(a.shape[0]) > 32:
             refuse(entry, f"{name} adapter rank {a.shape[0]} above 32")
-    if _padded_rank(ag.shape[0]) != _padded_rank(au.shape[0]):
+    if ag is not None and _padded_rank(ag.shape[0]) != _padded_rank(au.shape[0]):
         refuse(entry, "gate and up adapters must pad to the same rank")
     with torch.cuda.device(x.device):
         return _FusedMLP.apply(x, scaling, gp, gs, ag, bg, up_p, us, au, bu, dp, ds, ad, bd)

@@ -11,6 +11,8 @@ Targets:
 
   transformers.models.qwen2.modeling_qwen2   Qwen2RMSNorm.forward -> rms_norm;
                                               Qwen2DecoderLayer.forward (decoder.py);
+                                              Qwen2MLP.forward -> fused NF4 MLP (mlp.py);
+                                              apply_rotary_pos_emb -> fused q/k RoPE (rope.py);
                                               Qwen2ForCausalLM.forward -> fused head, no logits
   peft.tuners.lora.bnb                        Linear4bit.forward -> fused NF4 + LoRA (lora.py)
   bitsandbytes(.functional, .backends.cuda.ops)  NF4 decode and matmul_4bit (nf4_patch.py)
@@ -119,7 +121,11 @@ def _patch_qwen2(module):
     _replace(lm_cls, lambda original: _causal_lm_forward(original, lm_cls))
     _replace(norm_cls, _norm_forward)
     from .decoder import patch_qwen2_decoder
+    from .mlp import patch_qwen2_mlp
+    from .rope import patch_qwen2_rope
     patch_qwen2_decoder(module)
+    patch_qwen2_mlp(module)
+    patch_qwen2_rope(module)
 
 
 def _patch_peft(module):

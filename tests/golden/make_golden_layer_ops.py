@@ -1,4 +1,4 @@
-"""Golden vectors of the reference's RoPE and SwiGLU kernels (run once, here).
+"""Golden vectors of the reference's RoPE, SwiGLU and unpad code (run once, here).
 
 Usage (in a container where the reference checkout exists):
 
@@ -12,7 +12,10 @@ their wrappers under the Triton interpreter on CPU tensors:
   shapes and dtype combinations of solution/tests/test_rope.py:51-56, with the
   transposed [B, S, H, D] projection view and a broadcast or per-batch cos/sin;
 * ``swiglu_tile_engine`` (solution/kernels/swiglu_fused.py:21-46, launched as in
-  :53-78) forward and backward on fp16 gate/up [37, 300] and [3, 2304].
+  :53-78) forward and backward on fp16 gate/up [37, 300] and [3, 2304];
+* the unpad helpers (solution/unpad.py: ``right_padding_lengths`` :51-72,
+  ``_batch_metadata`` :164-183, ``_indices_from_lengths`` :186-200, ``_pack`` /
+  ``_scatter`` :149-161) on valid and invalid masks and a small hidden tensor.
 
 Inputs are stored with the outputs in ``golden_layer_ops.npz``; nothing at test
 time reads the reference.
@@ -86,6 +89,43 @@ def main(reference_root: str) -> None:
                                     BACKWARD=True, ROWS=4, COLS=256)
         for key, t in (("gate", g), ("up", u), ("act", a), ("grad", da), ("dgate", dg), ("dup", du)):
             arrays[f"swiglu_{name}_{key}"] = t.numpy()
+
+    # Unpad metadata and packing (solution/unpad.py:51-72, :149-200) on masks that
+    # are valid, non-binary, left-padded, with a label on padding, with an empty
+    # row, and as fp32 values; then pack/scatter of a [B, S, 3] tensor.
+    from solution import unpad as up
+    masks = {
+        "valid": ([[1, 1, 1, 0, 0], [1, 1, 1, 1, 1], [1, 0, 0, 0, 0]], None),
+        "nonbinary": ([[1, 2, 0, 0, 0], [1, 1, 1, 1, 1], [1, 0, 0, 0, 0]], None),
+        "leftpad": ([[0, 1, 1, 0, 0], [1, 1, 1, 1, 1], [1, 0, 0, 0, 0]], None),
+        "labelpad": ([[1, 1, 1, 0, 0], [1, 1, 1, 1, 1], [1, 0, 0, 0, 0]], (0, 4)),
+        "empty": ([[1, 1, 1, 0, 0], [0, 0, 0, 0, 0], [1, 0, 0, 0, 0]], None),
+    }
+    for name, (rows, bad_label) in masks.items():
+        mask = torch.tensor(rows, dtype=torch.int64)
+        labels = torch.where(mask == 1, torch.arange(mask.numel()).reshape(mask.shape), torch.full_like(mask, -100))
+        if bad_label is not None:
+            labels[bad_label] = 7
+        meta = up._batch_metadata(mask, labels)
+        lengths = up.right_padding_lengths(meta) if meta is not None else None
+        arrays[f"unpad_{name}_mask"] = mask.numpy()
+        arrays[f"unpad_{name}_labels"] = labels.numpy()
+        arrays[f"unpad_{name}_lengths"] = np.array(lengths if lengths is not None else [], dtype=np.int64)
+    float_mask = torch.tensor(masks["valid"][0], dtype=torch.float32)
+    arrays["unpad_float_lengths"] = np.array(up.right_padding_lengths(
+        up._batch_metadata(float_mask, torch.zeros_like(float_mask, dtype=torch.int64) - 100)), dtype=np.int64)
+    lengths = up.right_padding_lengths(masks["valid"][0])
+    indices = up._indices_from_lengths(lengths, 5, "cpu")
+
+    class _Batch:
+        batch, sequence, tokens = 3, 5, sum(lengths)
+    _Batch.indices = indices
+    x = torch.randn(3, 5, 3)
+    packed = up._pack(x, _Batch)
+    arrays["unpad_valid_indices"] = indices.numpy()
+    arrays["unpad_valid_x"] = x.numpy()
+    arrays["unpad_valid_packed"] = packed.numpy()
+    arrays["unpad_valid_scattered"] = up._scatter(packed, _Batch).numpy()
 
     np.savez_compressed(HERE / "golden_layer_ops.npz", **arrays)
     print("wrote", HERE / "golden_layer_ops.npz", (HERE / "golden_layer_ops.npz").stat().st_size, "bytes")

@@ -53,3 +53,27 @@ def test_swiglu_oracle_matches_reference_kernel(g, case):
     dg, du = O.swiglu_backward(p("gate"), p("up"), p("grad"))
     assert _ulps(dg, p("dgate")).max() <= 1
     assert _ulps(du, p("dup")).max() <= 1
+
+
+@pytest.mark.parametrize("case", ["valid", "nonbinary", "leftpad", "labelpad", "empty"])
+def test_unpad_oracle_matches_reference_metadata(g, case):
+    p = lambda key: g[f"unpad_{case}_{key}"]
+    got = O.unpad_lengths(p("mask"), p("labels"))
+    ref = tuple(int(x) for x in p("lengths"))
+    assert (got is None and ref == ()) or got == ref
+
+
+def test_unpad_oracle_pack_scatter_and_float_mask(g):
+    lengths = O.unpad_lengths(g["unpad_valid_mask"], g["unpad_valid_labels"])
+    assert np.array_equal(O.unpad_indices(lengths, 5), g["unpad_valid_indices"])
+    packed = O.unpad_pack(g["unpad_valid_x"], lengths)
+    assert np.array_equal(packed, g["unpad_valid_packed"][0])  # the reference packs to [1, T, ...]
+    assert np.array_equal(O.unpad_scatter(packed, lengths, 5), g["unpad_valid_scattered"])
+    assert O.unpad_lengths(g["unpad_valid_mask"].astype(np.float32)) == tuple(g["unpad_float_lengths"])
+
+
+def test_host_right_padding_check_matches_oracle(g):
+    from soupsuck_b200.unpad import right_padding_lengths
+    for case in ("valid", "nonbinary", "leftpad", "empty"):
+        mask = g[f"unpad_{case}_mask"]
+        assert right_padding_lengths(mask.tolist()) == O.unpad_lengths(mask)

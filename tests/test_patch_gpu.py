@@ -259,3 +259,55 @@ def test_qwen2_patched_loss_and_gradients_match_original(monkeypatch):
         assert rel < 2e-2, rel
     step = getattr(model, patch._MODEL_STEP)
     assert step is not None and int(step.labelled) == int((labels[:, 1:] != -100).sum())
+
+
+def test_qwen2_mlp_patch_runs_fused_mlp_on_nf4_projections(monkeypatch, fake_bnb_linear):
+    """Qwen2MLP with frozen bitsandbytes NF4 projections (the reference task's MLP:
+    LoRA only on q/v) runs the fused MLP; output and input gradient match the
+    original forward on the same decoded weights."""
+    import transformers
+    from transformers.models.qwen2 import modeling_qwen2 as q
+
+    from soupsuck_b200 import _lib
+    from soupsuck_b200.mlp import _MARKER, patch_qwen2_mlp
+
+    current = q.Qwen2MLP.forward
+    original = getattr(current, _MARKER, current)
+    monkeypatch.setattr(q.Qwen2MLP, "forward", original)
+    config = transformers.Qwen2Config(hidden_size=512, intermediate_size=1280, hidden_act="silu")
+    torch.manual_seed(11)
+    mlp = q.Qwen2MLP(config).cuda()
+    for key in ("gate_proj", "up_proj", "down_proj"):
+        lin = getattr(mlp, key)
+        setattr(mlp, key, fake_bnb_linear((lin.weight.detach() * 0.5).half()).cuda())
+    x = torch.randn((3, 100, 512), device="cuda", dtype=torch.float16, requires_grad=True)
+    dy = torch.randn((3, 100, 512), device="cuda", dtype=torch.float16)
+    ref = original(mlp, x)
+    ref.backward(dy)
+    ref_dx, x.grad = x.grad, None
+    assert patch_qwen2_mlp(q) and getattr(q.Qwen2MLP.forward, _MARKER) is original
+    before = _lib.launch_count()
+    out = mlp(x)
+    assert _lib.launch_count() > before
+    out.backward(dy)
+    _gate(out.float(), ref.float())
+    rel = (x.grad.double() - ref_dx.double()).norm() / ref_dx.double().norm()
+    assert rel < 5e-3, rel
+
+
+def test_qwen2_rope_patch_is_bit_exact_with_eager(monkeypatch):
+    from transformers.models.qwen2 import modeling_qwen2 as q
+
+    from soupsuck_b200.rope import _MARKER, patch_qwen2_rope
+
+    current = q.apply_rotary_pos_emb
+    original = getattr(current, _MARKER, current)
+    monkeypatch.setattr(q, "apply_rotary_pos_emb", original)
+    assert patch_qwen2_rope(q) and getattr(q.apply_rotary_pos_emb, _MARKER) is original
+    qs = torch.randn(2, 40, 12, 128, device="cuda", dtype=torch.float16).transpose(1, 2)
+    ks = torch.randn(2, 40, 2, 128, device="cuda", dtype=torch.float16).transpose(1, 2)
+    cos, sin = torch.randn(2, 40, 128, device="cuda"), torch.randn(2, 40, 128, device="cuda")
+    got = q.apply_rotary_pos_emb(qs, ks, cos, sin)
+    ref = original(qs, ks, cos, sin)
+    for a, b in zip(got, ref):
+        assert a.dtype == b.dtype and torch.equal(a.contiguous(), b.contiguous())
