@@ -320,6 +320,38 @@ def run_reference(args, torch):
 
 
 # ------------------------------------------------------------------ GPU timing helpers
+def mlp_calls(torch, layer, device, t, rnd):
+    """(label, launch) pairs of the fused MLP's four GEMM launches at T = t with
+    LoRA (rank-32 step for the gate/up pair, rank 16 for down)."""
+    import ctypes
+
+    from soupsuck_b200 import _lib
+    from soupsuck_b200.kernels.nf4_gemm import _weight_struct, nf4_linear_raw
+    calls = []
+    stream = _lib.stream_of(device)
+    wg = _weight_struct(layer["gate"][0], layer["gate"][1])
+    wu = _weight_struct(layer["up"][0], layer["up"][1])
+    dp, ds, da_, db_ = layer["down"]
+    wd = _weight_struct(dp, ds)
+    x, dy = rnd(t, HIDDEN), rnd(t, HIDDEN)
+    z2, b_gu, u2, at_cat = rnd(t, 2 * RANK_R), rnd(2 * INTER, 2 * RANK_R), rnd(t, 2 * RANK_R), rnd(HIDDEN, 2 * RANK_R)
+    zd, bd16, ud, atd = rnd(t, RANK_R), db_.detach().half().contiguous(), rnd(t, RANK_R), da_.detach().half().t().contiguous()
+    gate_up, act, dgu = rnd(t, 2 * INTER), rnd(t, INTER), rnd(t, 2 * INTER)
+    dx = torch.empty((t, HIDDEN), device=device, dtype=torch.float16)
+    nbytes = _lib.query("sb_nf4_linear_dx2_workspace_bytes", t, INTER, HIDDEN)
+    ws = torch.empty(max(nbytes, 1), device=device, dtype=torch.uint8)
+    calls.append(("gate/up fwd + SwiGLU", lambda: _lib.call("sb_nf4_mlp_gate_up_fwd", x.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
+                                   z2.data_ptr(), b_gu.data_ptr(), 2 * RANK_R, gate_up.data_ptr(), act.data_ptr(),
+                                   stream)))
+    calls.append(("down fwd", lambda: nf4_linear_raw(act, dp, ds, lora_a=zd, lora_b=bd16)))
+    calls.append(("down dX + SwiGLU'", lambda: _lib.call("sb_nf4_mlp_down_dx", dy.data_ptr(), t, ctypes.byref(wd), ud.data_ptr(),
+                                   atd.data_ptr(), RANK_R, gate_up.data_ptr(), dgu.data_ptr(), stream)))
+    calls.append(("gate/up dX (two weights)", lambda: _lib.call("sb_nf4_linear_dx2", dgu.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
+                                   u2.data_ptr(), at_cat.data_ptr(), 2 * RANK_R, dx.data_ptr(), ws.data_ptr(),
+                                   nbytes, stream)))
+    return calls
+
+
 def gemm_roofline(torch, layer, device, t, passes=10, warm=3):
     """Time the fused NF4 GEMM launches of one layer step back to back with CUDA
     events on their stream: forward and dX of q, k, v, o (LoRA fused) and the
@@ -343,27 +375,7 @@ def gemm_roofline(torch, layer, device, t, passes=10, warm=3):
                       nf4_linear_raw(x, p, s, lora_a=za, lora_b=bt)))
         calls.append((f"{name} dX", lambda dy=dy, p=packed, s=st, za=za, at=at:
                       nf4_linear_raw(dy, p, s, transpose=True, lora_a=za, lora_b=at)))
-    stream = _lib.stream_of(device)
-    wg = _weight_struct(layer["gate"][0], layer["gate"][1])
-    wu = _weight_struct(layer["up"][0], layer["up"][1])
-    dp, ds, da_, db_ = layer["down"]
-    wd = _weight_struct(dp, ds)
-    x, dy = rnd(t, HIDDEN), rnd(t, HIDDEN)
-    z2, b_gu, u2, at_cat = rnd(t, 2 * RANK_R), rnd(2 * INTER, 2 * RANK_R), rnd(t, 2 * RANK_R), rnd(HIDDEN, 2 * RANK_R)
-    zd, bd16, ud, atd = rnd(t, RANK_R), db_.detach().half().contiguous(), rnd(t, RANK_R), da_.detach().half().t().contiguous()
-    gate_up, act, dgu = rnd(t, 2 * INTER), rnd(t, INTER), rnd(t, 2 * INTER)
-    dx = torch.empty((t, HIDDEN), device=device, dtype=torch.float16)
-    nbytes = _lib.query("sb_nf4_linear_dx2_workspace_bytes", t, INTER, HIDDEN)
-    ws = torch.empty(max(nbytes, 1), device=device, dtype=torch.uint8)
-    calls.append(("gate/up fwd + SwiGLU", lambda: _lib.call("sb_nf4_mlp_gate_up_fwd", x.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
-                                   z2.data_ptr(), b_gu.data_ptr(), 2 * RANK_R, gate_up.data_ptr(), act.data_ptr(),
-                                   stream)))
-    calls.append(("down fwd", lambda: nf4_linear_raw(act, dp, ds, lora_a=zd, lora_b=bd16)))
-    calls.append(("down dX + SwiGLU'", lambda: _lib.call("sb_nf4_mlp_down_dx", dy.data_ptr(), t, ctypes.byref(wd), ud.data_ptr(),
-                                   atd.data_ptr(), RANK_R, gate_up.data_ptr(), dgu.data_ptr(), stream)))
-    calls.append(("gate/up dX (two weights)", lambda: _lib.call("sb_nf4_linear_dx2", dgu.data_ptr(), t, ctypes.byref(wg), ctypes.byref(wu),
-                                   u2.data_ptr(), at_cat.data_ptr(), 2 * RANK_R, dx.data_ptr(), ws.data_ptr(),
-                                   nbytes, stream)))
+    calls += mlp_calls(torch, layer, device, t, rnd)
     flops = step_flops(t)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for _ in range(warm):
@@ -457,6 +469,14 @@ def kernel_case(args, torch):
             call = lambda: nf4_linear_raw(x, packed, st, transpose=True, lora_a=za, lora_b=la)
         for _ in range(args.warmup + args.steps):
             call()
+    elif args.kernel_case == "mlp":
+        layer = build_layer(torch, device, seed=0)
+        gen = torch.Generator(device=device).manual_seed(5)
+        rnd = lambda *shape: torch.randn(shape, device=device, dtype=torch.float16, generator=gen)
+        calls = mlp_calls(torch, layer, device, t, rnd)
+        for _ in range(args.warmup + args.steps):
+            for _, c in calls:
+                c()
     elif args.kernel_case == "gemm_pass":
         layer = build_layer(torch, device, seed=0)
         gemm_roofline(torch, layer, device, t, passes=args.steps, warm=args.warmup)
@@ -824,7 +844,7 @@ def main():
     ap.add_argument("--workload", choices=["layer", "sweep", "stack"], default="layer",
                     help="layer: configs[1] (the headline line); sweep: configs[4] 7B shapes; "
                          "stack: configs[2] 28-layer stack, data parallel")
-    ap.add_argument("--kernel-case", choices=["nf4_fwd", "nf4_dx", "gemm_pass", "layer", "ce"],
+    ap.add_argument("--kernel-case", choices=["nf4_fwd", "nf4_dx", "gemm_pass", "mlp", "layer", "ce"],
                     help="run a small launch of one kernel family (for ncu) instead of the bench")
     ap.add_argument("--case-n", type=int, default=INTER)
     ap.add_argument("--case-k", type=int, default=HIDDEN)
@@ -932,6 +952,9 @@ def main():
             for _ in range(2):
                 g_.replay()
         torch.cuda.synchronize()
+        # Only the `graphs` list may own the captured steps: they hold NCCL work and
+        # must all be released before the process group is destroyed.
+        del g_
     graph = graphs[0] if graphs else None
 
     def run_step():
@@ -1045,6 +1068,9 @@ def main():
     graph = None
     graphs.clear()
     graph_grads.clear()
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     if rank != 0:
         if dist is not None:
             dist.barrier()

@@ -124,6 +124,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
 // ----------------------------------------------------------------- 2-SM pair launch
 constexpr int kPairStages = 6;         // dX, and the stream-K forward
 constexpr int kPairFwdTileStages = 4;  // whole-tile forward (leaves room for store staging)
+constexpr int kPairMlpBwdStages = 4;   // down dX + SwiGLU derivatives (room for the gate/up box sets)
 
 template <int BMODE, int EMODE, int STAGES, bool SK, int WSEL = 0>
 inline int configure_pair(const char* name) {
@@ -322,6 +323,7 @@ inline int nf4_linear_tc(bool dx, const uint16_t* act, int64_t m, const sb_nf4_w
   p.lora_r = r;
   if (pl.streamk && pl.pair) {
     p.streamk = 1;
+    p.nfast = 1;
     p.partials = static_cast<float*>(workspace);
     p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
                                         align256(static_cast<size_t>(pl.grid) * 2 * pair::kSlotF4 * sizeof(float4)));
@@ -454,11 +456,14 @@ inline int mlp_down_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight& wd, c
                        cudaStream_t stream) {
   const int64_t red = wd.n_out, n = wd.k_in;
   const int64_t m_tiles = (m + pair::kTileM - 1) / pair::kTileM, n_tiles = (n + pair::kTileN - 1) / pair::kTileN;
-  CUtensorMap ta, tb, tla, tlb, ty;
+  CUtensorMap ta, tb, tla, tlb, ty, tgu;
   int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dy, red, m, red * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wd.packed, n / 2, red, n / 2, kNF4BN / 2, 64,
                          CU_TENSOR_MAP_SWIZZLE_64B);
   if (!rc) rc = make_map(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dgate_up, 2 * n, m, 4 * n, 64, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  // The epilogue loads the saved gate/up in the same 32-row x 64-column boxes.
+  if (!rc) rc = make_map(&tgu, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, gate_up, 2 * n, m, 4 * n, 64, 32,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   tla = ta;
@@ -487,8 +492,8 @@ inline int mlp_down_dx(const uint16_t* dy, int64_t m, const sb_nf4_weight& wd, c
   const int64_t tiles = m_tiles * n_tiles;
   const int slots = pair_slots();
   const int grid = 2 * static_cast<int>(tiles < slots ? tiles : slots);
-  return launch_pair_sk<kNF4Dx, kSwiGLUBwd, kPairStages, false, 0>(ta, tb, tla, tlb, ty, p, grid, stream,
-                                                                    "nf4_mlp_down_dx");
+  return launch_pair_sk<kNF4Dx, kSwiGLUBwd, kPairMlpBwdStages, false, 0>(ta, tb, tla, tlb, ty, p, grid, stream,
+                                                                          "nf4_mlp_down_dx", &tgu, nullptr);
 }
 
 // dX[m, K] = dY2[m, 2N] . [deq(W1); deq(W2)] (+ lora_a [m, r] . lora_b[K, r]^T): the input
@@ -549,6 +554,7 @@ inline int linear_dx2(const uint16_t* dy2, int64_t m, const sb_nf4_weight& w1, c
   p.ldo = k;
   if (pl.streamk) {
     p.streamk = 1;
+    p.nfast = 1;
     p.partials = static_cast<float*>(workspace);
     p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
                                         align256(static_cast<size_t>(pl.grid) * 2 * pair::kSlotF4 * sizeof(float4)));

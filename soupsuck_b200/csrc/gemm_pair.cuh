@@ -98,6 +98,10 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                "r"(smem_addr(src)), "r"(x), "r"(y)
                : "memory");
 }
+// Pull one 128-byte line toward L2 ahead of its use (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most one committed store group still reads shared memory.
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
@@ -193,7 +197,9 @@ struct PairCfg {
   // Epilogue staging: per epilogue warp two 32-row x 64-column fp16 boxes (SW128);
   // three for the SwiGLU forward, whose panels go out as gate, up and activation.
   static constexpr int kStoreBoxBytes = 32 * 64 * 2;
-  static constexpr int kBoxes = EMODE == kSwiGLUFwd ? 3 : 2;
+  // ... and four (two gate/up sets loaded ahead and rewritten in place) for the
+  // SwiGLU backward.
+  static constexpr int kBoxes = EMODE == kSwiGLUFwd ? 3 : (EMODE == kSwiGLUBwd ? 4 : 2);
   static constexpr int kStagingBytes = kStoreStage ? 4 * kBoxes * kStoreBoxBytes : 0;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + kBarrierBytes + 1024;
   static_assert(STAGES % 2 == 0, "two decoder groups alternate stages: each stage keeps one group");
@@ -204,6 +210,17 @@ struct PairCfg {
   static_assert(EMODE != kSwiGLUBwd || BMODE == kNF4Dx, "SwiGLU backward: dX epilogue");
 };
 
+// Tile coordinates: m-fastest, or n-fastest when p.nfast is set.  Under the
+// stream-K schedule consecutive pairs then hold the N-tiles of one M-tile at k
+// positions a few dozen blocks apart, so a long reduction's A operand is reread
+// from L2 rather than from DRAM (A of a [3300, 17920] input is 118 MB).
+__device__ __forceinline__ int tile_m(const Params& p, int tile) {
+  return p.nfast ? tile / p.n_tiles : tile % p.m_tiles;
+}
+__device__ __forceinline__ int tile_n(const Params& p, int tile) {
+  return p.nfast ? tile % p.n_tiles : tile / p.m_tiles;
+}
+
 // Stream-K partial slot of one CTA: [chunk 8][float4 8][thread 128], 128 KB.
 constexpr int kSlotF4 = (kTileN / 32) * 8 * 128;
 
@@ -211,11 +228,13 @@ constexpr int kSlotF4 = (kTileN / 32) * 8 * 128;
 // Warps 4..7 of each CTA: rows m0 + 128 * rank + 32 * (warp % 4) + lane, all 256
 // columns of the tile.  Releases go to rank 0's acc_empty.
 // STAGE: the kernel has store staging (bulk-store epilogue available).
+// tmAux: the kSwiGLUFwd activation map, or the kSwiGLUBwd gate/up map; gu_full:
+// that mode's two box-set barriers per epilogue warp.
 template <int EMODE, bool SK, bool STAGE>
-__device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap* tmY, const CUtensorMap* tmY2,
+__device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap* tmY, const CUtensorMap* tmAux,
                                               uint8_t* staging,
                                               uint32_t tmem_base, uint64_t* acc_full,
-                                              uint32_t leader_acc_empty, uint64_t* epi_mb,
+                                              uint32_t leader_acc_empty, uint64_t* epi_mb, uint64_t* gu_full,
                                               volatile int* abort_flag, volatile int* last_flag, int warp,
                                               int lane, int num_tiles, int rows_valid, int pair_id, int pairs,
                                               uint32_t rank) {
@@ -225,17 +244,61 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
   uint32_t tl = 0, epi_phase = 0, boxes = 0;
   int uidx = 0;
   // This warp's staging boxes; rows of a box are this warp's 32 TMEM lanes.
-  constexpr int kBoxes = EMODE == kSwiGLUFwd ? 3 : 2;
-  uint8_t* my_boxes = staging + (warp - 4) * kBoxes * (32 * 64 * 2);
+  // The SwiGLU backward keeps two sets of (gate, up) boxes that its TMA loads
+  // fill one panel ahead and that it overwrites in place with (dgate, dup).
+  constexpr int kBoxes = EMODE == kSwiGLUFwd ? 3 : (EMODE == kSwiGLUBwd ? 4 : 2);
+  constexpr int kBoxBytes = 32 * 64 * 2;
+  uint8_t* my_boxes = staging + (warp - 4) * kBoxes * kBoxBytes;
+  // kSwiGLUBwd box-set bookkeeping: pc counts this warp's panels; set pc & 1,
+  // its barrier phase (pc >> 1) & 1; pending[s]: a load into set s not yet waited.
+  uint32_t pc = 0;
+  bool pending[2] = {false, false};
+  uint64_t* my_gu = gu_full + (warp - 4) * 2;
+  auto gu_issue = [&](uint32_t pcx, int col, int row0) {
+    const uint32_t set = pcx & 1u;
+    if (lane == 0) {
+      uint8_t* b = my_boxes + set * 2 * kBoxBytes;
+      mbar_arrive_expect_tx(&my_gu[set], 2 * kBoxBytes);
+      tma_load_2d(b, tmAux, &my_gu[set], col, row0);
+      tma_load_2d(b + kBoxBytes, tmAux, &my_gu[set], p.N + col, row0);
+    }
+    pending[set] = true;
+  };
+  // Wait out every load still aimed at this warp's boxes (bounded; used on exit paths).
+  auto gu_drain = [&]() {
+    volatile int no_abort = 0;
+    for (uint32_t d = 0; d < 2; ++d) {
+      const uint32_t pcx = pc + d;
+      if (pending[pcx & 1u] && lane == 0) mbar_wait(&my_gu[pcx & 1u], (pcx >> 1) & 1u, kErrWaitDrain, &no_abort);
+      pending[pcx & 1u] = false;
+    }
+    __syncwarp();
+  };
   UnitIter iter(p, num_tiles, pair_id, pairs);
   Unit u;
   while (iter.next(u)) {
-    const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
+    const int mt = tile_m(p, u.tile), nt = tile_n(p, u.tile);
     const int m0 = mt * kTileM, n0 = nt * kTileN;
     if (m0 >= rows_valid) continue;
     const int buf = tl & 1;
     const uint32_t aph = (tl >> 1) & 1;
-    if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) break;
+    if constexpr (EMODE == kSwiGLUBwd) {
+      // Panel 0's gate/up boxes do not depend on the accumulator: request them
+      // before waiting for it (the other box set may still feed the previous
+      // panel's stores; this set's last stores must have read it).
+      const int npanels = (p.N - n0 < kTileN ? p.N - n0 : kTileN) / 64;
+      if (npanels > 0) {
+        if (lane == 0) bulk_wait_read1();
+        __syncwarp();
+        gu_issue(pc, n0, m0 + static_cast<int>(rank) * kTileRows + q * 32);
+      }
+      if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) {
+        gu_drain();
+        break;
+      }
+    } else if (!mbar_wait(&acc_full[buf], aph, kErrWaitAccFull, abort_flag)) {
+      break;
+    }
     tc_fence_after();
     const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * kTileN;
     const int row = m0 + static_cast<int>(rank) * kTileRows + q * 32 + lane;
@@ -286,7 +349,7 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
         if (lane == 0) {
           tma_store_2d(tmY, box_g, oc0 + panel * 64, row0);
           tma_store_2d(tmY, box_u, p.N + oc0 + panel * 64, row0);
-          tma_store_2d(tmY2, box_a, oc0 + panel * 64, row0);
+          tma_store_2d(tmAux, box_a, oc0 + panel * 64, row0);
           bulk_commit();
         }
       }
@@ -296,61 +359,74 @@ __device__ __forceinline__ void pair_epilogue(const Params& p, const CUtensorMap
       // Down-projection dX tile: the accumulator is dL/d(act) for columns
       // n0 .. n0+256 of this CTA's 128 rows.  Rounded to fp16 (the down
       // projection's input-gradient dtype), it meets the saved gate / up values
-      // of the same positions; dgate goes to columns [0, N) and dup to [N, 2N)
-      // of the [M, 2N] output.  Rows past M read nothing (their stores are
-      // clipped by the tensor map); N is a multiple of 64.
+      // of the same positions, which TMA has brought into this warp's box set
+      // one panel ahead; dgate and dup overwrite them in place and go out to
+      // columns [0, N) and [N, 2N) of the [M, 2N] output.  Rows past M load
+      // zeros and are clipped from the stores; N is a multiple of 64.
       const int row0 = m0 + static_cast<int>(rank) * kTileRows + q * 32;
       const uint32_t swz = static_cast<uint32_t>(lane & 7);
-      uint8_t* box_dg = my_boxes;
-      uint8_t* box_du = my_boxes + 32 * 64 * 2;
-      const bool row_ok = row < p.M;
-      const __half* grow = p.gu + static_cast<int64_t>(row_ok ? row : 0) * p.ld_gu;
+      const int npanels = (p.N - n0 < kTileN ? p.N - n0 : kTileN) / 64;
+      bool ok_tile = true;
 #pragma unroll 1
-      for (int panel = 0; panel < kTileN / 64; ++panel) {
+      for (int panel = 0; panel < npanels; ++panel) {
         const int c_panel = n0 + panel * 64;
-        if (c_panel >= p.N) break;
-        if (lane == 0) bulk_wait_read0();
-        __syncwarp();
+        if (panel + 1 < npanels) {
+          // The next panel's set last fed the previous panel's stores.
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          gu_issue(pc + 1, c_panel + 64, row0);
+        }
+        const uint32_t set = pc & 1u;
+        if (!warp_wait(&my_gu[set], (pc >> 1) & 1u, kErrWaitFull, abort_flag, lane)) {
+          ok_tile = false;
+          break;
+        }
+        pending[set] = false;
+        uint8_t* box_g = my_boxes + set * 2 * kBoxBytes;
+        uint8_t* box_u = box_g + kBoxBytes;
 #pragma unroll 1
         for (int half = 0; half < 2; ++half) {
-          const int c0 = c_panel + half * 32;
           uint32_t v[32];
           tmem_ld32(tacc + panel * 64 + half * 32, v);
-          uint4 gw[4], uw[4];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            gw[c] = row_ok ? __ldg(reinterpret_cast<const uint4*>(grow + c0) + c) : make_uint4(0, 0, 0, 0);
-            uw[c] = row_ok ? __ldg(reinterpret_cast<const uint4*>(grow + p.N + c0) + c) : make_uint4(0, 0, 0, 0);
-          }
           tmem_ld_wait();
-          const __half2* g2 = reinterpret_cast<const __half2*>(gw);
-          const __half2* u2 = reinterpret_cast<const __half2*>(uw);
-          uint32_t hdg[16], hdu[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float2 da = __half22float2(__floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
-            const float2 gf = __half22float2(g2[j]), uf = __half22float2(u2[j]);
-            float dg0, du0, dg1, du1;
-            swiglu::backward(gf.x, uf.x, da.x, dg0, du0);
-            swiglu::backward(gf.y, uf.y, da.y, dg1, du1);
-            __half2 dg = __floats2half2_rn(dg0, dg1), du = __floats2half2_rn(du0, du1);
-            hdg[j] = *reinterpret_cast<uint32_t*>(&dg);
-            hdu[j] = *reinterpret_cast<uint32_t*>(&du);
-          }
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const uint32_t off = lane * 128 + ((static_cast<uint32_t>(half * 4 + c) ^ swz) << 4);
-            *reinterpret_cast<uint4*>(box_dg + off) = make_uint4(hdg[4 * c], hdg[4 * c + 1], hdg[4 * c + 2], hdg[4 * c + 3]);
-            *reinterpret_cast<uint4*>(box_du + off) = make_uint4(hdu[4 * c], hdu[4 * c + 1], hdu[4 * c + 2], hdu[4 * c + 3]);
+            uint4 gw = *reinterpret_cast<const uint4*>(box_g + off);
+            uint4 uw = *reinterpret_cast<const uint4*>(box_u + off);
+            const __half2* g2 = reinterpret_cast<const __half2*>(&gw);
+            const __half2* u2 = reinterpret_cast<const __half2*>(&uw);
+            uint32_t hdg[4], hdu[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int e = 8 * c + 2 * j;
+              const float2 da = __half22float2(__floats2half2_rn(__uint_as_float(v[e]), __uint_as_float(v[e + 1])));
+              const float2 gf = __half22float2(g2[j]), uf = __half22float2(u2[j]);
+              float dg0, du0, dg1, du1;
+              swiglu::backward(gf.x, uf.x, da.x, dg0, du0);
+              swiglu::backward(gf.y, uf.y, da.y, dg1, du1);
+              __half2 dg = __floats2half2_rn(dg0, dg1), du = __floats2half2_rn(du0, du1);
+              hdg[j] = *reinterpret_cast<uint32_t*>(&dg);
+              hdu[j] = *reinterpret_cast<uint32_t*>(&du);
+            }
+            *reinterpret_cast<uint4*>(box_g + off) = make_uint4(hdg[0], hdg[1], hdg[2], hdg[3]);
+            *reinterpret_cast<uint4*>(box_u + off) = make_uint4(hdu[0], hdu[1], hdu[2], hdu[3]);
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(tmY, box_dg, c_panel, row0);
-          tma_store_2d(tmY, box_du, p.N + c_panel, row0);
+          tma_store_2d(tmY, box_g, c_panel, row0);
+          tma_store_2d(tmY, box_u, p.N + c_panel, row0);
           bulk_commit();
         }
+        ++pc;
+      }
+      if (!ok_tile) {
+        gu_drain();
+        tc_fence_before();
+        mbar_arrive_cluster(leader_acc_empty + 8u * buf);
+        break;
       }
       tc_fence_before();
       mbar_arrive_cluster(leader_acc_empty + 8u * buf);
@@ -531,7 +607,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint64_t* epi_mb = drain + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(epi_mb + 1);
+  uint64_t* gu_full = epi_mb + 1;  // kSwiGLUBwd: two box-set barriers per epilogue warp
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gu_full + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* last_flag = abort_flag + 1;
   float* code2_s = reinterpret_cast<float*>(bar_area + 1024);
@@ -558,6 +635,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(epi_mb, 128);
+    for (int i = 0; i < 8; ++i) mbar_init(&gu_full[i], 1);
     *abort_flag = 0;
     *last_flag = 0;
     fence_barrier_init();
@@ -602,7 +680,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
       UnitIter iter(p, num_tiles, pair_id, pairs);
       Unit u;
       while (ok && iter.next(u)) {
-        const int mt = u.tile % p.m_tiles, nt = u.tile / p.m_tiles;
+        const int mt = tile_m(p, u.tile), nt = tile_n(p, u.tile);
         const int m0 = mt * kTileM;
         if (m0 >= rows_valid) continue;
         const int arow = m0 + static_cast<int>(rank) * kTileRows;
@@ -663,7 +741,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
       UnitIter iter(p, num_tiles, pair_id, pairs);
       Unit u;
       while (ok && iter.next(u)) {
-        if ((u.tile % p.m_tiles) * kTileM >= rows_valid) continue;
+        if (tile_m(p, u.tile) * kTileM >= rows_valid) continue;
         const int buf = tl & 1;
         const uint32_t aph = (tl >> 1) & 1;
         if (!warp_wait(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag, lane)) { ok = false; break; }
@@ -713,8 +791,10 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
     }
   } else if (warp >= 4 && warp < 8) {
     if (lane == 0 && C::kStoreStage && p.store_tma) tma_prefetch_desc(&tmY);
-    if (lane == 0 && EMODE == kSwiGLUFwd) tma_prefetch_desc(&tmY2);
-    pair_epilogue<EMODE, SK, C::kStoreStage>(p, &tmY, &tmY2, staging, tmem_base, acc_full, leader_acc_empty, epi_mb, abort_flag, last_flag, warp, lane,
+    const CUtensorMap* aux = EMODE == kSwiGLUBwd ? &tmB2 : &tmY2;
+    if (lane == 0 && (EMODE == kSwiGLUFwd || EMODE == kSwiGLUBwd)) tma_prefetch_desc(aux);
+    pair_epilogue<EMODE, SK, C::kStoreStage>(p, &tmY, aux, staging, tmem_base, acc_full, leader_acc_empty, epi_mb,
+                                             gu_full, abort_flag, last_flag, warp, lane,
                          num_tiles, rows_valid, pair_id, pairs, rank);
   } else if (warp >= 8) {
     // ------------------------------------------------------------ NF4 decoders (both CTAs)
@@ -774,8 +854,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
     UnitIter iter(p, num_tiles, pair_id, pairs);
     Unit u;
     while (ok && iter.next(u)) {
-      if ((u.tile % p.m_tiles) * kTileM >= rows_valid) continue;
-      const int nt = u.tile / p.m_tiles;
+      if (tile_m(p, u.tile) * kTileM >= rows_valid) continue;
+      const int nt = tile_n(p, u.tile);
       const int n0 = WSEL == 1 ? nt * kHalfN : nt * kTileN + static_cast<int>(rank) * kHalfN;
       const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
       const int first = u.k0 + ((static_cast<int>(it & 1) == group) ? 0 : 1);

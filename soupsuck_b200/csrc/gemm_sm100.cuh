@@ -52,6 +52,7 @@ struct Params {
   int vec_ok;             // output rows are 16-byte aligned
   int store_tma;          // 2-SM pair kernel: fp16 output written by bulk tensor stores
   int streamk;            // 1: stream-K schedule (equal k-iteration shares per CTA)
+  int nfast;              // 2-SM pair kernel: tiles numbered n-fastest (see tile_m / tile_n)
   int ksplit;             // whole-tile schedule: 2 splits every tile's reduction in two halves,
                           // the second half accumulating into out_split (0 or 1: no split)
   void* out_split;        // kAccF32 / kStoreF32 output of the second half

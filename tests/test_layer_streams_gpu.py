@@ -1,10 +1,10 @@
 """The benchmark's decoder-layer step with its independent projections on side
 streams gives the gradients of the one-stream step.
 
-bench.layer_step overlaps o/down, k/v and up with the main stream; autograd runs
-each backward node on its forward's stream.  Every kernel is deterministic, so
-the only difference allowed is the order in which autograd adds the input
-gradients of projections that share an input (q/k/v, gate/up): fp16 sums in a
+bench.layer_step overlaps o and k/v with the main stream; autograd runs each
+backward node on its forward's stream.  Every kernel is deterministic, so the
+only difference allowed is the order in which autograd adds the input
+gradients of projections that share an input (q/k/v): fp16 sums in a
 different order, compared at 1e-2 relative L2 of the fp16 gradients (a fraction
 of one fp16 ulp per add) and exactly for the LoRA weight gradients, whose
 reductions do not depend on the order of other streams.
@@ -18,14 +18,14 @@ pytestmark = pytest.mark.gpu
 
 
 def _run(bench, layer, inp, streams):
-    for name in ("residual", "attn", "act", "mlp_prev"):
+    for name in bench.DIFF_INPUTS:
         inp[name].grad = None
     params = bench.lora_params(layer)
     for p in params:
         p.grad = None
     bench.layer_step(torch, layer, inp, streams)
     torch.cuda.synchronize()
-    return ({name: inp[name].grad.clone() for name in ("residual", "attn", "act", "mlp_prev")},
+    return ({name: inp[name].grad.clone() for name in bench.DIFF_INPUTS},
             [p.grad.clone() for p in params])
 
 
@@ -37,7 +37,7 @@ def test_streamed_layer_step_matches_one_stream(tokens):
     g = torch.Generator(device=dev).manual_seed(6)
     inp = {name: torch.randn(shp, device=dev, dtype=torch.float16, generator=g)
            for name, shp in bench.input_shapes(tokens).items()}
-    for name in ("residual", "attn", "act", "mlp_prev"):
+    for name in bench.DIFF_INPUTS:
         inp[name].requires_grad_()
     ref_in, ref_p = _run(bench, layer, inp, None)
     streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
