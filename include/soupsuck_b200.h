@@ -119,6 +119,13 @@ size_t sb_nf4_linear_workspace_bytes(int64_t m, int64_t n_out, int64_t k_in, int
 int sb_lora_prepare(const void* a, int a_dtype, const void* b, int b_dtype, int r, int64_t k,
                     int64_t n, uint16_t* a16, uint16_t* at16, uint16_t* b16, uint16_t* bt16,
                     void* stream);
+/* sb_lora_prepare_pair: two adapters of one input (gate and up) as one rank-2r adapter:
+ *   a1, a2 [r, k] and b1, b2 [n, r] -> fp16 a_cat [2r, k] (a1 over a2), at_cat [k, 2r],
+ *   b_bd [2n, 2r] = [[b1, 0], [0, b2]] and bt_bd [2r, 2n].  No counterpart in the
+ *   reference, whose gate/up projections carry no adapters together. */
+int sb_lora_prepare_pair(const void* a1, const void* a2, int a_dtype, const void* b1, const void* b2,
+                         int b_dtype, int r, int64_t k, int64_t n, uint16_t* a_cat, uint16_t* at_cat,
+                         uint16_t* b_bd, uint16_t* bt_bd, void* stream);
 int sb_lora_project(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int r,
                     float scale_rows, uint16_t* out_rows, int ld_rows, float scale_t,
                     uint16_t* out_t, int64_t ldt, void* stream);

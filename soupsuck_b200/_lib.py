@@ -43,6 +43,7 @@ SIGNATURES = {
     "sb_nf4_linear_dx": (_I32, [_P, _I64, ctypes.POINTER(NF4Weight), _P, _P, _I32, _P, _P, _SZ, _P]),
     "sb_nf4_linear_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
     "sb_lora_prepare": (_I32, [_P, _I32, _P, _I32, _I32, _I64, _I64, _P, _P, _P, _P, _P]),
+    "sb_lora_prepare_pair": (_I32, [_P, _P, _I32, _P, _P, _I32, _I32, _I64, _I64, _P, _P, _P, _P, _P]),
     "sb_lora_project": (_I32, [_P, _I64, _I64, _P, _I32, _F32, _P, _I32, _F32, _P, _I64, _P]),
     "sb_lora_reduce_workspace_bytes": (_SZ, [_I64, _I64, _I32]),
     "sb_lora_reduce": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _F32, _I32, _P, _I32, _P, _SZ, _P]),

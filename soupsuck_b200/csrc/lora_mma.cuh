@@ -4,7 +4,8 @@
 // activation-sized matrix once, so they use register-fragment MMAs fed by wide
 // coalesced loads rather than the tcgen05 pipeline.
 //
-//   project  out[M, R] = X[M, K] . W[R, K]^T          (Z = X.A^T, U = dY.B)
+//   project  out[M, R] = X[M, K] . W[R, K]^T          (Z = X.A^T, U = dY.B);
+//            ranks 16 / 32 split the reduction over a cluster (project3)
 //            writes scale_rows * out as fp16 [M, rp] (row-major, the GEMM's
 //            LoRA operand) and/or scale_t * out^T as fp16 [R, ldt] (for the
 //            weight-gradient reductions).
@@ -149,6 +150,40 @@ __global__ void __launch_bounds__(256) reduce_finalize2_kernel(const float* __re
   }
 }
 
+// Finalize of the streamed reduction: one thread per four outputs adds the splits'
+// fp32 partials in split order (16-byte loads, four splits in flight), scales and
+// stores; enough threads for the whole output in one wave.
+__global__ void __launch_bounds__(256) reduce_finalize3_kernel(const float* __restrict__ partial, int splits,
+                                                               int64_t Wd, int r, float scale, int transpose,
+                                                               void* __restrict__ out, int odt) {
+  const int64_t total4 = Wd * r / 4;
+  const int64_t e4 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e4 >= total4) return;
+  const float4* src = reinterpret_cast<const float4*>(partial) + e4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int s = 0;
+  for (; s + 4 <= splits; s += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldcg(src + static_cast<int64_t>(s + u) * total4);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc.x += v[u].x; acc.y += v[u].y; acc.z += v[u].z; acc.w += v[u].w;
+    }
+  }
+  for (; s < splits; ++s) {
+    const float4 v = __ldcg(src + static_cast<int64_t>(s) * total4);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  const float vals[4] = {acc.x * scale, acc.y * scale, acc.z * scale, acc.w * scale};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t e = e4 * 4 + i;
+    const int64_t j = e / Wd, c = e % Wd;
+    st_from_f32(out, odt, transpose ? c * r + j : j * Wd + c, vals[i]);
+  }
+}
+
 // ------------------------------------------------------------------ streamed variants
 // The two kernels above keep few bytes in flight (4-byte loads in the reduction,
 // one 16-row tile of 4 warps in the projection).  The streamed variants below
@@ -240,6 +275,156 @@ __global__ void __launch_bounds__(256) project2_kernel(
       out_t[static_cast<int64_t>(col) * ldt + m] = __float2half_rn(0.0f);  // zero pad for the reduction
     }
   }
+}
+
+// project3: the projection for ranks <= 32 with the reduction split over a
+// cluster.  A cluster of S CTAs owns one block of 32 rows (two m16 tiles, so each
+// W fragment feeds two MMAs); CTA `rank` reduces columns [K*rank/S, K*(rank+1)/S)
+// with its 8 warps, the warps' partials meet in shared memory, and the S CTA
+// partials are added in rank order through distributed shared memory, each rank
+// finishing a share of the 32 x R outputs (fixed order: deterministic).  S is
+// chosen so that about four CTAs run per SM whatever the row count, which keeps
+// enough 16-byte loads in flight to stream X at HBM rate.
+constexpr int kProj3Rows = 32;
+constexpr int64_t kProj3MinK = 4096;  // rows at least this long take the cluster split
+
+template <int R>
+__global__ void __launch_bounds__(256) project3_kernel(
+    const __half* __restrict__ X, int64_t M, int64_t K, const __half* __restrict__ W, int S,
+    float scale_rows, __half* __restrict__ out_rows, int ld_rows, float scale_t,
+    __half* __restrict__ out_t, int64_t ldt) {
+  static_assert(R == 16 || R == 32, "cluster projection for ranks 16 and 32");
+  constexpr int NT = R / 8, MT = 2, kWarps = 8, kUnroll = 4;
+  __shared__ float red[kWarps][kProj3Rows][R + 1];
+  __shared__ float part[kProj3Rows * R];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t rank = gemm::pair::cluster_rank();
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x / S) * kProj3Rows;
+  const int64_t chunks = K / 32;
+  const int64_t cta_b = chunks * rank / S, cta_e = chunks * (rank + 1) / S;
+  const int64_t c_begin = cta_b + (cta_e - cta_b) * warp / kWarps;
+  const int64_t c_end = cta_b + (cta_e - cta_b) * (warp + 1) / kWarps;
+  float acc[MT][NT][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
+  const __half* xr[MT][2];
+  bool rok[MT][2];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t row = m0 + 16 * i + g + 8 * h;
+      rok[i][h] = row < M;
+      xr[i][h] = X + (rok[i][h] ? row : 0) * K + 8 * t;
+    }
+  const __half* wrow = W + static_cast<int64_t>(g) * K + 8 * t;
+  for (int64_t c = c_begin; c < c_end; c += kUnroll) {
+    uint4 xv[kUnroll][MT][2];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const bool in = c + u < c_end;
+      const int64_t k0 = (c + u) * 32;
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) xv[u][i][h] = ldg16_or_zero(xr[i][h] + k0, in && rok[i][h]);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (c + u < c_end) {
+        const int64_t k0 = (c + u) * 32;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const uint4 w = __ldg(reinterpret_cast<const uint4*>(wrow + static_cast<int64_t>(8 * j) * K + k0));
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            const uint32_t a_lo[4] = {xv[u][i][0].x, xv[u][i][1].x, xv[u][i][0].y, xv[u][i][1].y};
+            const uint32_t a_hi[4] = {xv[u][i][0].z, xv[u][i][1].z, xv[u][i][0].w, xv[u][i][1].w};
+            mma16816(acc[i][j], a_lo, w.x, w.y);
+            mma16816(acc[i][j], a_hi, w.z, w.w);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      red[warp][16 * i + g][8 * j + 2 * t] = acc[i][j][0];
+      red[warp][16 * i + g][8 * j + 2 * t + 1] = acc[i][j][1];
+      red[warp][16 * i + g + 8][8 * j + 2 * t] = acc[i][j][2];
+      red[warp][16 * i + g + 8][8 * j + 2 * t + 1] = acc[i][j][3];
+    }
+  __syncthreads();
+  for (int e = threadIdx.x; e < kProj3Rows * R; e += blockDim.x) {
+    const int row = e / R, col = e % R;
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += red[w][row][col];
+    part[e] = v;
+  }
+  gemm::pair::cluster_sync_all();
+  const uint32_t part_s = smem_addr(part);
+  const int total = kProj3Rows * R;
+  const int share = (total + S - 1) / S;
+  const int e0 = static_cast<int>(rank) * share;
+  const int e1 = e0 + share < total ? e0 + share : total;
+  for (int e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+    const int row = e / R, col = e % R;
+    float v = 0.0f;
+    for (int q = 0; q < S; ++q) {
+      const uint32_t addr = gemm::pair::map_to_rank(part_s + static_cast<uint32_t>(e * 4), static_cast<uint32_t>(q));
+      float pv;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(addr) : "memory");
+      v += pv;
+    }
+    const int64_t m = m0 + row;
+    if (m < M) {
+      if (out_rows) out_rows[m * ld_rows + col] = __float2half_rn(v * scale_rows);
+      if (out_t) out_t[static_cast<int64_t>(col) * ldt + m] = __float2half_rn(v * scale_t);
+    } else if (out_t && m < ldt) {
+      out_t[static_cast<int64_t>(col) * ldt + m] = __float2half_rn(0.0f);  // zero pad for the reduction
+    }
+  }
+  gemm::pair::cluster_sync_all();  // no CTA leaves while a peer still reads its partial
+}
+
+// Cluster size of project3 for m rows and k columns (see above).
+inline int project3_split(int64_t m, int64_t k) {
+  const int64_t blocks = (m + kProj3Rows - 1) / kProj3Rows;
+  const int64_t want = (4 * static_cast<int64_t>(device_sm_count()) + blocks - 1) / blocks;
+  int64_t s = want < 8 ? want : 8;
+  const int64_t cap = k / 32 / 32;  // every warp keeps at least four 32-column chunks
+  if (s > cap) s = cap;
+  return static_cast<int>(s < 1 ? 1 : s);
+}
+
+template <int R>
+inline int launch_project3(const __half* X, int64_t m, int64_t k, const __half* W, float scale_rows, __half* orow,
+                           int ld_rows, float scale_t, __half* ot, int64_t ldt, cudaStream_t st) {
+  const int S = project3_split(m, k);
+  const int64_t blocks = (m + kProj3Rows - 1) / kProj3Rows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks * S), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, project3_kernel<R>, X, m, k, W, S, scale_rows, orow, ld_rows, scale_t,
+                                     ot, ldt);
+  if (e != cudaSuccess) return fail(SB_ECUDA, std::string("lora_project3 launch: ") + cudaGetErrorString(e));
+  count_launch();
+  return check_launch("lora_project3_kernel");
 }
 
 // reduce2: CTA = 256 output columns (8 warps x 32) over rows [split * rows_per_split, ...).
@@ -396,6 +581,36 @@ __global__ void prepare_kernel(const void* __restrict__ a, int adt, const void* 
   }
 }
 
+// Two adapters of one input as one rank-2r adapter: a1, a2 [r, K] and b1, b2 [N, r]
+// (dtype adt / bdt) -> a_cat [2r, K] (a1 over a2), at_cat [K, 2r], b_bd [2N, 2r]
+// = [[b1, 0], [0, b2]] and bt_bd [2r, 2N] (its transpose), fp16, zero blocks
+// written too.  One pass over every output element.
+__global__ void pair_prepare_kernel(const void* __restrict__ a1, const void* __restrict__ a2, int adt,
+                                    const void* __restrict__ b1, const void* __restrict__ b2, int bdt, int r,
+                                    int64_t K, int64_t N, __half* __restrict__ a_cat, __half* __restrict__ at_cat,
+                                    __half* __restrict__ b_bd, __half* __restrict__ bt_bd) {
+  const int64_t na = 2 * static_cast<int64_t>(r) * K;
+  const int64_t nb = 2 * N * 2 * static_cast<int64_t>(r);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < na + nb; i += stride) {
+    if (i < na) {
+      const int64_t j = i / K, k = i % K;  // j in [0, 2r)
+      const bool second = j >= r;
+      const __half v = __float2half_rn(ld_as_f32(second ? a2 : a1, adt, (second ? j - r : j) * K + k));
+      a_cat[i] = v;
+      at_cat[k * 2 * r + j] = v;
+    } else {
+      const int64_t ib = i - na;
+      const int64_t n2 = ib / (2 * r), c = ib % (2 * r);  // row of b_bd, column in [0, 2r)
+      const bool row2 = n2 >= N, col2 = c >= r;
+      __half v = __float2half_rn(0.0f);
+      if (row2 == col2) v = __float2half_rn(ld_as_f32(row2 ? b2 : b1, bdt, (row2 ? n2 - N : n2) * r + (col2 ? c - r : c)));
+      b_bd[ib] = v;
+      bt_bd[c * 2 * N + n2] = v;
+    }
+  }
+}
+
 template <int R>
 inline int launch_reduce2(dim3 grid, const __half* P, int64_t ldp, const __half* Q, int64_t m, int64_t w,
                           int64_t rows_per_split, float* partial, cudaStream_t st) {
@@ -449,6 +664,12 @@ int sb_lora_project(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, 
   const __half* W = reinterpret_cast<const __half*>(w);
   __half* orow = reinterpret_cast<__half*>(out_rows);
   __half* ot = reinterpret_cast<__half*>(out_t);
+  // Long rows (the MLP's act, dgate|dup) take the cluster-split kernel; short rows
+  // (hidden-size inputs) keep one 16-row tile per CTA, which already yields more
+  // CTAs than SMs and no cluster exchange.
+  const bool split = k >= sb::lora::kProj3MinK;
+  if (r == 16 && split) return sb::lora::launch_project3<16>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt, st);
+  if (r == 32 && split) return sb::lora::launch_project3<32>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt, st);
   if (r == 16) sb::lora::project2_kernel<16><<<grid, 256, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
   else if (r == 32) sb::lora::project2_kernel<32><<<grid, 256, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
   else sb::lora::project2_kernel<64><<<grid, 256, 0, st>>>(X, m, k, W, scale_rows, orow, ld_rows, scale_t, ot, ldt);
@@ -510,11 +731,18 @@ int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m
     if (int rc = sb::check_launch("lora_reduce_partial_kernel")) return rc;
   }
   const int64_t total = w * r;
-  if (w % 4 == 0) {
+  if (w % 4 == 0 && splits >= 16) {
+    // Many splits over few outputs: spread the splits over 16 thread groups.
     sb::lora::reduce_finalize2_kernel<<<static_cast<unsigned>((total / 4 + 15) / 16), 256, 0, st>>>(
         partial, splits, w, r, scale, transpose, out, out_dtype);
     sb::count_launch();
     return sb::check_launch("lora_reduce_finalize2_kernel");
+  }
+  if (w % 4 == 0) {
+    sb::lora::reduce_finalize3_kernel<<<static_cast<unsigned>((total / 4 + 255) / 256), 256, 0, st>>>(
+        partial, splits, w, r, scale, transpose, out, out_dtype);
+    sb::count_launch();
+    return sb::check_launch("lora_reduce_finalize3_kernel");
   }
   sb::lora::reduce_finalize_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
       partial, splits, w, r, scale, transpose, out, out_dtype);
@@ -536,6 +764,22 @@ int sb_lora_prepare(const void* a, int a_dtype, const void* b, int b_dtype, int 
       reinterpret_cast<__half*>(b16), reinterpret_cast<__half*>(bt16));
   sb::count_launch();
   return sb::check_launch("lora_prepare_kernel");
+}
+
+int sb_lora_prepare_pair(const void* a1, const void* a2, int a_dtype, const void* b1, const void* b2,
+                         int b_dtype, int r, int64_t k, int64_t n, uint16_t* a_cat, uint16_t* at_cat,
+                         uint16_t* b_bd, uint16_t* bt_bd, void* stream) {
+  SB_REQUIRE(r > 0 && k > 0 && n > 0, "expected positive sizes");
+  SB_REQUIRE((a_dtype == SB_F16 || a_dtype == SB_F32) && (b_dtype == SB_F16 || b_dtype == SB_F32), "bad dtype");
+  SB_REQUIRE(a1 && a2 && b1 && b2 && a_cat && at_cat && b_bd && bt_bd, "NULL pointer argument");
+  const int64_t total = 2 * static_cast<int64_t>(r) * k + 4 * n * static_cast<int64_t>(r);
+  const int64_t blocks = (total + 255) / 256;
+  const int grid = static_cast<int>(blocks < 4096 ? blocks : 4096);
+  sb::lora::pair_prepare_kernel<<<grid, 256, 0, sb::as_stream(stream)>>>(
+      a1, a2, a_dtype, b1, b2, b_dtype, r, k, n, reinterpret_cast<__half*>(a_cat), reinterpret_cast<__half*>(at_cat),
+      reinterpret_cast<__half*>(b_bd), reinterpret_cast<__half*>(bt_bd));
+  sb::count_launch();
+  return sb::check_launch("lora_pair_prepare_kernel");
 }
 
 }  // extern "C"

@@ -83,18 +83,35 @@ def swiglu_fused_backward(gate, up, grad, gate_dtype=None, up_dtype=None):
 class _PairFactors:
     """The gate and up adapters as one rank-2r adapter (rp = padded rank):
     a_cat [2rp, H] (both A stacked), at_cat [H, 2rp], b_gu [2N, 2rp] = [Bg 0; 0 Bu],
-    bt_bd [2rp, 2N] = [Bg^T 0; 0 Bu^T]."""
+    bt_bd [2rp, 2N] = [Bg^T 0; 0 Bu^T].  Built by one sb_lora_prepare_pair launch
+    when both ranks equal the padded rank and the factors share dtypes; otherwise
+    from the per-adapter fp16 copies."""
 
-    def __init__(self, fg, fu):
-        rp, n = fg.rp, fg.b16.shape[0]
-        dev = fg.a16.device
-        self.rp, self.r_gate, self.r_up = rp, fg.r, fu.r
-        self.a_cat = torch.cat([fg.a16, fu.a16])
-        self.at_cat = torch.cat([fg.at16, fu.at16], dim=1)
-        self.b_gu = torch.zeros((2 * n, 2 * rp), device=dev, dtype=HALF)
+    def __init__(self, ag, bg, au, bu):
+        r, h = ag.shape
+        n = bg.shape[0]
+        rp = _padded_rank(r)
+        dev = ag.device
+        self.rp, self.r_gate, self.r_up = rp, r, au.shape[0]
+        self.a_cat = torch.empty((2 * rp, h), device=dev, dtype=HALF)
+        self.at_cat = torch.empty((h, 2 * rp), device=dev, dtype=HALF)
+        self.b_gu = torch.empty((2 * n, 2 * rp), device=dev, dtype=HALF)
+        self.bt_bd = torch.empty((2 * rp, 2 * n), device=dev, dtype=HALF)
+        direct = (r == rp and au.shape[0] == rp and ag.dtype == au.dtype and bg.dtype == bu.dtype)
+        if direct:
+            tensors = [t.detach().contiguous() for t in (ag, au, bg, bu)]
+            _lib.call("sb_lora_prepare_pair", tensors[0].data_ptr(), tensors[1].data_ptr(),
+                      _lib.dtype_code(ag.dtype), tensors[2].data_ptr(), tensors[3].data_ptr(),
+                      _lib.dtype_code(bg.dtype), rp, h, n, self.a_cat.data_ptr(), self.at_cat.data_ptr(),
+                      self.b_gu.data_ptr(), self.bt_bd.data_ptr(), _lib.stream_of(dev))
+            return
+        fg, fu = _factors(ag, bg), _factors(au, bu)
+        torch.cat([fg.a16, fu.a16], out=self.a_cat)
+        torch.cat([fg.at16, fu.at16], dim=1, out=self.at_cat)
+        self.b_gu.zero_()
         self.b_gu[:n, :rp] = fg.b16
         self.b_gu[n:, rp:] = fu.b16
-        self.bt_bd = torch.zeros((2 * rp, 2 * n), device=dev, dtype=HALF)
+        self.bt_bd.zero_()
         self.bt_bd[:rp, :n] = fg.bt16
         self.bt_bd[rp:, n:] = fu.bt16
 
@@ -103,17 +120,20 @@ _PAIR_CACHE = {}
 
 
 def _pair_factors(ag, bg, au, bu):
-    fg, fu = _factors(ag, bg), _factors(au, bu)
+    """Cached like _factors: reused while the four parameters are unchanged (same
+    storage and version counters); rebuilt inside every CUDA-graph capture."""
     if torch.cuda.is_current_stream_capturing():
-        return _PairFactors(fg, fu)
-    key = (id(fg), id(fu))
+        return _PairFactors(ag, bg, au, bu)
+    key = tuple(id(t) for t in (ag, bg, au, bu))
+    stamp = tuple((t.data_ptr(), t._version, t.dtype, tuple(t.shape)) for t in (ag, bg, au, bu))
+    stamp += (torch.cuda.current_stream(ag.device).cuda_stream,)
     hit = _PAIR_CACHE.get(key)
-    if hit is not None and hit[0]() is fg and hit[1]() is fu:
+    if hit is not None and hit[0] == stamp and all(ref() is t for ref, t in zip(hit[1], (ag, bg, au, bu))):
         return hit[2]
-    pf = _PairFactors(fg, fu)
+    pf = _PairFactors(ag, bg, au, bu)
     if len(_PAIR_CACHE) > 1024:
         _PAIR_CACHE.clear()
-    _PAIR_CACHE[key] = (weakref.ref(fg), weakref.ref(fu), pf)
+    _PAIR_CACHE[key] = (stamp, tuple(weakref.ref(t) for t in (ag, bg, au, bu)), pf)
     return pf
 
 
