@@ -89,10 +89,11 @@ def pass_bytes(m):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one 12-launch GEMM
-# pass, from a separate ncu capture of `bench.py --kernel-case gemm_pass` (ncu
-# cannot run inside the timed bench).  A static figure: it is reported as such
-# and describes the kernels of the capture it came from.
-PASS_TRAFFIC_NCU = {}
+# pass, from a separate ncu capture of `bench.py --kernel-case gemm_pass --warmup 1
+# --steps 1` (-k regex:pair_kernel -s 12 -c 12; ncu cannot run inside the timed
+# bench).  A static figure: it is reported as such and describes the kernels of
+# the capture it came from (626.0 MB read + 226.8 MB written).
+PASS_TRAFFIC_NCU = {3300: 852767232}
 
 
 def static_pass_traffic(m):
@@ -1104,7 +1105,7 @@ def main():
         "gpu_launches": int(launches_per_step) * args.steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_burst, "unit": "TFLOP/s",
                      "frac": achieved / peak_burst, "traffic": static_pass_traffic(t),
-                     "traffic_source": "static ncu figure (DRAM bytes per pass of the 14 launches, "
+                     "traffic_source": "static ncu figure (DRAM bytes per pass of the 12 launches, "
                                        "captured separately from this run)",
                      "algorithmic_bytes": pass_bytes(t),
                      "kernel": "pair_kernel<NF4> (cta_group::2): q/k/v/o fwd+dX, MLP gate/up+SwiGLU, down, "
