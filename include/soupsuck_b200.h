@@ -133,6 +133,28 @@ size_t sb_lora_reduce_workspace_bytes(int64_t m, int64_t w, int r);
 int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m, int64_t w, int r,
                    float scale, int transpose, void* out, int out_dtype, void* workspace,
                    size_t workspace_bytes, void* stream);
+/* sb_lora_dual: the two products of the LoRA backward that read the upstream
+ * gradient Q = dY [m, w] (16-byte aligned, w % 8 == 0), from one pass over it:
+ *   dB = scale_b * Pt . Q  (Pt = Z^T [r, ldp], rows m..ldp-1 zero), [r, w] or
+ *        transposed [w, r], in db_dtype -- the sb_lora_reduce of dB;
+ *   U  = Q . Bt^T          (Bt [r, w]), fp16(scale_rows * U) row-major with pitch
+ *        ld_rows and/or fp16(scale_t * U)^T [r, ldt] (ldt = m rounded up to 16,
+ *        rows m..ldt-1 zero) -- the sb_lora_project of U.
+ * wsplit = 0: dense, r = 16 or 32.  wsplit > 0 (a multiple of 256): two adapters
+ * side by side (the gate/up pair, r = 32 or 64): columns below wsplit pair with
+ * factor rows [0, r/2), the others with [r/2, r); U is the full product (Bt's
+ * off-diagonal blocks are zero) and dB only its diagonal blocks, [r/2, w] (or
+ * [w, r/2]) with each column's rows counted from its block's first.
+ * pt = NULL: U only (db_out unused) -- the forward's Z = X.A^T for long rows.
+ * Deterministic; workspace sb_lora_dual_workspace_bytes(m, w, r, wsplit).
+ * Replaces the projection + reduction pair of the LoRA backward
+ * (solution/lora.py:161 under autograd: lora_B's weight gradient and input
+ * gradient read the same upstream gradient). */
+size_t sb_lora_dual_workspace_bytes(int64_t m, int64_t w, int r, int64_t wsplit);
+int sb_lora_dual(const uint16_t* q, int64_t m, int64_t w, const uint16_t* pt, int64_t ldp, const uint16_t* bt,
+                 int r, int64_t wsplit, float scale_b, int transpose_b, void* db_out, int db_dtype,
+                 float scale_rows, uint16_t* u_rows, int ld_rows, float scale_t, uint16_t* u_t, int64_t ldt,
+                 void* workspace, size_t workspace_bytes, void* stream);
 /* sb_lora_reduce without any allocation or workspace, for callers that cannot
  * allocate device memory (memory planned once at start-up, foreign-language
  * bindings without a CUDA allocator, steps that must not grow their footprint).

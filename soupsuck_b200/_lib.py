@@ -47,6 +47,9 @@ SIGNATURES = {
     "sb_lora_project": (_I32, [_P, _I64, _I64, _P, _I32, _F32, _P, _I32, _F32, _P, _I64, _P]),
     "sb_lora_reduce_workspace_bytes": (_SZ, [_I64, _I64, _I32]),
     "sb_lora_reduce": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _F32, _I32, _P, _I32, _P, _SZ, _P]),
+    "sb_lora_dual_workspace_bytes": (_SZ, [_I64, _I64, _I32, _I64]),
+    "sb_lora_dual": (_I32, [_P, _I64, _I64, _P, _I64, _P, _I32, _I64, _F32, _I32, _P, _I32,
+                            _F32, _P, _I32, _F32, _P, _I64, _P, _SZ, _P]),
     "sb_lora_reduce_static": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _F32, _I32, _P, _I32, _P]),
     "sb_lora_scale_add": (_I32, [_P, _I32, _P, _I32, _P, _I32, _I64, _F32, _I32, _P]),
     "sb_lora_scale_grad": (_I32, [_P, _I32, _P, _I32, _I64, _F32, _P]),

@@ -632,6 +632,284 @@ inline int launch_reduce2(dim3 grid, const __half* P, int64_t ldp, const __half*
   return check_launch("lora_reduce2_kernel");
 }
 
+// ------------------------------------------------------------------ dual
+// The LoRA backward reads its upstream gradient Q = dY [M, W] for two products:
+// u = Q . Bt^T [M, r] (the rank-r factor of the input gradient and of dA) and
+// dB = Pt . Q [r, W] with Pt = Z^T (the forward's rank-r factor, transposed).  For
+// the MLP's dgate|dup that is 118 MB per read.  dual_kernel streams every
+// [32 x 256] tile of Q once, through the reduce2 ring, into both:
+//   * dB: the CTA's 256 columns over its row split, as reduce2 (partials per
+//     split, summed by the reduce finalize kernels);
+//   * u: the tile's 32 rows over the CTA's 256 columns, from the CTA's block of Bt
+//     held in shared memory; written per column block and summed by
+//     dual_u_finalize_kernel.
+// Block-diagonal mode (wsplit > 0: two adapters side by side, the gate/up pair):
+// columns below wsplit use factor rows [0, RH) of Pt and Bt, the others rows
+// [RH, 2 RH); only those diagonal blocks are computed -- u's off-diagonal blocks
+// multiply zeros, and dB's are not wanted.  wsplit is a multiple of 256, so a
+// column block lies on one side.
+// Warps for u: (m16 tile mi, group nq of RH/16 n8 tiles, column half kh), the two
+// column halves added in fixed order through shared memory.  DB = false: u only
+// (the forward's Z = X.A^T for long rows), without Pt, dB or its partials.
+template <int RH>
+struct DualSmem {
+  static constexpr int kStage = Red2Smem<RH>::kStage;
+  static constexpr int kRing = kRedStages * kStage;
+  static constexpr int kBtBytes = RH * kRedCols * 2;           // the CTA's Bt block
+  static constexpr int kXchBytes = 2 * 4 * 32 * (RH / 4) * 4;  // two tiles' column-half partials
+  static constexpr int kBytes = kRing + kBtBytes + kXchBytes;
+};
+
+template <int RH, bool DB>
+__global__ void __launch_bounds__(256) dual_kernel(
+    const __half* __restrict__ Pt, int64_t ldp, const __half* __restrict__ Bt, int64_t ldb,
+    const __half* __restrict__ Q, int64_t M, int64_t Wd, int64_t wsplit, int64_t rows_end,
+    int64_t rows_per_split, float* __restrict__ partial, float* __restrict__ upart, int64_t ldq) {
+  using S = DualSmem<RH>;
+  constexpr int MT = RH / 16;  // dB: m16 tiles of factor rows
+  constexpr int NPW = RH / 16; // u: n8 tiles per warp
+  extern __shared__ __align__(128) uint8_t dual_smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kRedCols;
+  const int64_t jbase = (wsplit > 0 && c0 >= wsplit) ? RH : 0;
+  const int64_t mb = static_cast<int64_t>(blockIdx.y) * rows_per_split;
+  int64_t me = mb + rows_per_split;
+  if (me > rows_end) me = rows_end;
+  const int ntiles = me > mb ? static_cast<int>((me - mb + kRedRows - 1) / kRedRows) : 0;
+  const uint32_t sbase = smem_addr(dual_smem);
+  const uint32_t bts = sbase + S::kRing;
+  float* xch = reinterpret_cast<float*>(dual_smem + S::kRing + S::kBtBytes);
+
+  auto issue = [&](int tile) {
+    const int slot = tile % kRedStages;
+    const uint32_t qs = sbase + slot * S::kStage;
+    const uint32_t ps = qs + Red2Smem<RH>::kQBytes;
+    const int64_t r0 = mb + static_cast<int64_t>(tile) * kRedRows;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int row = (tid >> 5) + 8 * u, chunk = tid & 31;
+      const int64_t m = r0 + row, col = c0 + chunk * 8;
+      const bool ok = m < M && col < Wd;
+      cp_async16(qs + row * 512 + ((chunk ^ (row & 7)) << 4), ok ? Q + m * Wd + col : Q, ok);
+    }
+    if constexpr (DB) {
+      for (int i = tid; i < 4 * RH; i += 256) {
+        const int j = i >> 2, chunk = i & 3;
+        const int64_t tok = r0 + chunk * 8;
+        const bool ok = tok < ldp;
+        cp_async16(ps + j * 64 + ((chunk ^ ((j >> 1) & 3)) << 4), ok ? Pt + (jbase + j) * ldp + tok : Pt, ok);
+      }
+    }
+  };
+
+  // The CTA's Bt block (rows jbase .. jbase + RH, its 256 columns): part of group 0.
+  for (int i = tid; i < RH * 32; i += 256) {
+    const int j = i >> 5, chunk = i & 31;
+    const int64_t col = c0 + chunk * 8;
+    const bool ok = col < Wd;
+    cp_async16(bts + j * 512 + ((chunk ^ (j & 7)) << 4), ok ? Bt + (jbase + j) * ldb + col : Bt, ok);
+  }
+
+  float acc[MT][4][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int n = 0; n < 4; ++n) acc[i][n][0] = acc[i][n][1] = acc[i][n][2] = acc[i][n][3] = 0.0f;
+
+#pragma unroll
+  for (int s = 0; s < kRedStages - 1; ++s) {
+    if (s < ntiles) issue(s);
+    cp_async_commit();
+  }
+  const int mat = lane >> 3, r8 = lane & 7;
+  const int mi = warp & 1, nq = (warp >> 1) & 1, kh = warp >> 2;
+  const int64_t ublock = static_cast<int64_t>(blockIdx.x) * ldq;
+  for (int tile = 0; tile < ntiles; ++tile) {
+    cp_async_wait<kRedStages - 2>();
+    __syncthreads();
+    if (tile + kRedStages - 1 < ntiles) issue(tile + kRedStages - 1);
+    cp_async_commit();
+    const int slot = tile % kRedStages;
+    const uint32_t qs = sbase + slot * S::kStage;
+    const uint32_t ps = qs + Red2Smem<RH>::kQBytes;
+    // dB += Pt[:, tile rows] . Q[tile rows, warp's 32 columns]
+#pragma unroll
+    for (int ks = 0; ks < (DB ? 2 : 0); ++ks) {
+      uint32_t a[MT][4];
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        const int j = 16 * i + r8 + 8 * (mat & 1);
+        const int chunk = 2 * ks + (mat >> 1);
+        ldsm_x4(ps + j * 64 + ((chunk ^ ((j >> 1) & 3)) << 4), a[i]);
+      }
+      uint32_t b[2][4];
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {
+        const int k = 16 * ks + r8 + 8 * (mat & 1);
+        const int chunk = warp * 4 + 2 * pr + (mat >> 1);
+        ldsm_x4_trans(qs + k * 512 + ((chunk ^ (k & 7)) << 4), b[pr]);
+      }
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          mma16816(acc[i][2 * pr], a[i], b[pr][0], b[pr][1]);
+          mma16816(acc[i][2 * pr + 1], a[i], b[pr][2], b[pr][3]);
+        }
+      }
+    }
+    // u[tile rows 16 mi .., n8 tiles of group nq] over column half kh
+    float uacc[NPW][4];
+#pragma unroll
+    for (int n = 0; n < NPW; ++n) uacc[n][0] = uacc[n][1] = uacc[n][2] = uacc[n][3] = 0.0f;
+    const int arow = 16 * mi + r8 + 8 * (mat & 1);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int cb = kh * 16 + kk * 4;  // first 16-byte chunk of this pair of k16 steps
+      uint32_t a0[4], a1[4];
+      ldsm_x4(qs + arow * 512 + (((cb + (mat >> 1)) ^ (arow & 7)) << 4), a0);
+      ldsm_x4(qs + arow * 512 + (((cb + 2 + (mat >> 1)) ^ (arow & 7)) << 4), a1);
+#pragma unroll
+      for (int n = 0; n < NPW; ++n) {
+        const int j = 8 * (nq * NPW + n) + r8;
+        uint32_t bb[4];
+        ldsm_x4(bts + j * 512 + (((cb + mat) ^ (j & 7)) << 4), bb);
+        mma16816(uacc[n], a0, bb[0], bb[1]);
+        mma16816(uacc[n], a1, bb[2], bb[3]);
+      }
+    }
+    float* x = xch + ((tile & 1) * 4 + (warp & 3)) * 32 * (RH / 4) + lane * (RH / 4);
+    if (kh == 1) {
+#pragma unroll
+      for (int n = 0; n < NPW; ++n)
+        *reinterpret_cast<float4*>(x + 4 * n) = make_float4(uacc[n][0], uacc[n][1], uacc[n][2], uacc[n][3]);
+    }
+    __syncthreads();
+    if (kh == 0) {
+      const int64_t r0 = mb + static_cast<int64_t>(tile) * kRedRows + 16 * mi + g;
+#pragma unroll
+      for (int n = 0; n < NPW; ++n) {
+        const float4 o = *reinterpret_cast<const float4*>(x + 4 * n);
+        const int j = 8 * (nq * NPW + n) + 2 * t;
+        if (r0 < ldq)
+          *reinterpret_cast<float2*>(upart + (ublock + r0) * RH + j) = make_float2(uacc[n][0] + o.x, uacc[n][1] + o.y);
+        if (r0 + 8 < ldq)
+          *reinterpret_cast<float2*>(upart + (ublock + r0 + 8) * RH + j) =
+              make_float2(uacc[n][2] + o.z, uacc[n][3] + o.w);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if constexpr (DB) {
+    float* out = partial + static_cast<int64_t>(blockIdx.y) * RH * Wd;
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int64_t col = c0 + warp * 32 + 8 * n + 2 * t;
+        if (col < Wd) {
+          const int64_t ra = 16 * i + g;
+          *reinterpret_cast<float2*>(out + ra * Wd + col) = make_float2(acc[i][n][0], acc[i][n][1]);
+          *reinterpret_cast<float2*>(out + (ra + 8) * Wd + col) = make_float2(acc[i][n][2], acc[i][n][3]);
+        }
+      }
+    }
+  }
+}
+
+// u[m, j] = fp16(scale * sum of upart[cb][m][j mod RH] over the column blocks of
+// j's side), rows m < M into out_rows [M, ld_rows], and transposed into out_t
+// [rout, ldt] with zeros for rows M .. ldt.  A CTA: 8 groups x 32 float4 outputs;
+// group q adds blocks q, q + 8, ... and the group sums are added in group order.
+__global__ void __launch_bounds__(256) dual_u_finalize_kernel(
+    const float* __restrict__ upart, int nblocks, int split_block, int64_t ldq, int rh, int rout, int64_t M,
+    float scale_rows, __half* __restrict__ out_rows, int ld_rows, float scale_t, __half* __restrict__ out_t,
+    int64_t ldt) {
+  __shared__ float4 part[8][33];
+  const int col = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int q4 = rout / 4;
+  const int64_t total4 = ldq * q4;
+  const int64_t e4 = static_cast<int64_t>(blockIdx.x) * 32 + col;
+  const int64_t m = e4 / q4;
+  const int j = static_cast<int>(e4 % q4) * 4;
+  const int side = (split_block > 0 && j >= rh) ? 1 : 0;
+  const int lo = side ? split_block : 0;
+  const int hi = (split_block > 0 && !side) ? split_block : nblocks;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (e4 < total4) {
+    const int jj = j - side * rh;
+    for (int cb = lo + grp; cb < hi; cb += 8) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(upart + (static_cast<int64_t>(cb) * ldq + m) * rh + jj));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+  }
+  part[grp][col] = acc;
+  __syncthreads();
+  if (grp != 0 || e4 >= total4) return;
+  float4 s = part[0][col];
+#pragma unroll
+  for (int q = 1; q < 8; ++q) {
+    const float4 v = part[q][col];
+    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+  }
+  const float vals[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (m < M) {
+      if (out_rows) out_rows[m * ld_rows + j + i] = __float2half_rn(vals[i] * scale_rows);
+      if (out_t) out_t[static_cast<int64_t>(j + i) * ldt + m] = __float2half_rn(vals[i] * scale_t);
+    } else if (out_t && m < ldt) {
+      out_t[static_cast<int64_t>(j + i) * ldt + m] = __float2half_rn(0.0f);
+    }
+  }
+}
+
+template <int RH, bool DB>
+inline int launch_dual(dim3 grid, const __half* P, int64_t ldp, const __half* Bt, int64_t ldb, const __half* Q,
+                       int64_t m, int64_t w, int64_t wsplit, int64_t rows_end, int64_t rows_per_split,
+                       float* partial, float* upart, int64_t ldq, cudaStream_t st) {
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(dual_kernel<RH, DB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           DualSmem<RH>::kBytes);
+      if (e != cudaSuccess) return fail(SB_ECUDA, std::string("dual smem attribute: ") + cudaGetErrorString(e));
+      configured[dev] = true;
+    }
+  }
+  dual_kernel<RH, DB><<<grid, 256, DualSmem<RH>::kBytes, st>>>(P, ldp, Bt, ldb, Q, m, w, wsplit, rows_end,
+                                                             rows_per_split, partial, upart, ldq);
+  count_launch();
+  return check_launch("lora_dual_kernel");
+}
+
+// Row plan of dual_kernel for m rows and w columns: (splits, rows per split), the
+// splits as reduce2's, over the 16-row padded length.
+struct DualPlan {
+  int64_t ldq, rows_per_split;
+  int splits, nblocks;
+  size_t partial_bytes, upart_bytes;
+};
+
+inline DualPlan dual_plan(int64_t m, int64_t w, int rh) {
+  DualPlan d{};
+  d.ldq = (m + 15) / 16 * 16;
+  int s = reduce2_splits(d.ldq, w);
+  int64_t rps = (d.ldq + s - 1) / s;
+  rps = (rps + kRedRows - 1) / kRedRows * kRedRows;
+  d.rows_per_split = rps;
+  d.splits = static_cast<int>((d.ldq + rps - 1) / rps);
+  d.nblocks = static_cast<int>((w + kRedCols - 1) / kRedCols);
+  d.partial_bytes = (static_cast<size_t>(d.splits) * rh * w * sizeof(float) + 255) / 256 * 256;
+  d.upart_bytes = static_cast<size_t>(d.nblocks) * d.ldq * rh * sizeof(float);
+  return d;
+}
+
 inline int reduce_splits(int64_t m, int64_t w) {
   const int64_t col_blocks = (w + 127) / 128;
   int64_t s = (2 * device_sm_count() + col_blocks - 1) / col_blocks;
@@ -748,6 +1026,85 @@ int sb_lora_reduce(const uint16_t* pt, int64_t ldp, const uint16_t* q, int64_t m
       partial, splits, w, r, scale, transpose, out, out_dtype);
   sb::count_launch();
   return sb::check_launch("lora_reduce_finalize_kernel");
+}
+
+size_t sb_lora_dual_workspace_bytes(int64_t m, int64_t w, int r, int64_t wsplit) {
+  if (m <= 0 || w <= 0 || r <= 0) return 0;
+  const int rh = wsplit > 0 ? r / 2 : r;
+  const sb::lora::DualPlan d = sb::lora::dual_plan(m, w, rh);
+  return d.partial_bytes + d.upart_bytes;
+}
+
+int sb_lora_dual(const uint16_t* q, int64_t m, int64_t w, const uint16_t* pt, int64_t ldp, const uint16_t* bt,
+                 int r, int64_t wsplit, float scale_b, int transpose_b, void* db_out, int db_dtype,
+                 float scale_rows, uint16_t* u_rows, int ld_rows, float scale_t, uint16_t* u_t, int64_t ldt,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  SB_REQUIRE(m >= 0 && w > 0, "expected m >= 0 and w > 0");
+  SB_REQUIRE(w % 8 == 0, "w must be a multiple of 8");
+  SB_REQUIRE(wsplit >= 0 && wsplit < w, "wsplit must be in [0, w)");
+  if (wsplit > 0) {
+    SB_REQUIRE(wsplit % sb::lora::kRedCols == 0, "wsplit must be a multiple of 256");
+    SB_REQUIRE(r == 32 || r == 64, "block-diagonal rank must be 32 or 64 (two halves of 16 or 32)");
+  } else {
+    SB_REQUIRE(r == 16 || r == 32, "rank must be 16 or 32 (pad smaller ranks with zeros)");
+  }
+  SB_REQUIRE(!pt || (ldp >= m && ldp % 16 == 0), "ldp must be >= m and a multiple of 16 (zero padded)");
+  SB_REQUIRE(!pt || db_dtype == SB_F16 || db_dtype == SB_F32, "bad dB dtype");
+  SB_REQUIRE(!u_rows || ld_rows >= r, "ld_rows must be >= r");
+  SB_REQUIRE(!u_t || (ldt >= m && ldt <= (m + 15) / 16 * 16), "ldt must be m rounded up to at most 16");
+  SB_REQUIRE(!pt || db_out != nullptr, "NULL dB output");
+  const int rh = wsplit > 0 ? r / 2 : r;
+  cudaStream_t st = sb::as_stream(stream);
+  if (m == 0) {
+    if (!pt) return SB_OK;
+    cudaError_t e = cudaMemsetAsync(db_out, 0, static_cast<size_t>(rh) * w * (db_dtype == SB_F32 ? 4 : 2), st);
+    return e == cudaSuccess ? SB_OK : sb::fail(SB_ECUDA, cudaGetErrorString(e));
+  }
+  SB_REQUIRE(q && bt && (u_rows || u_t), "NULL pointer argument");
+  SB_REQUIRE(sb::aligned(q, 16) && sb::aligned(bt, 16) && (!pt || sb::aligned(pt, 16)),
+             "q, pt and bt must be 16-byte aligned");
+  const sb::lora::DualPlan d = sb::lora::dual_plan(m, w, rh);
+  if (!workspace || workspace_bytes < d.partial_bytes + d.upart_bytes)
+    return sb::fail(SB_EWORKSPACE, "LoRA dual workspace too small");
+  float* partial = static_cast<float*>(workspace);
+  float* upart = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + d.partial_bytes);
+  const __half* P = reinterpret_cast<const __half*>(pt);
+  const __half* B = reinterpret_cast<const __half*>(bt);
+  const __half* Q = reinterpret_cast<const __half*>(q);
+  dim3 grid(static_cast<unsigned>(d.nblocks), static_cast<unsigned>(d.splits));
+  int rc;
+  if (P) {
+    rc = rh == 16 ? sb::lora::launch_dual<16, true>(grid, P, ldp, B, w, Q, m, w, wsplit, d.ldq, d.rows_per_split,
+                                                    partial, upart, d.ldq, st)
+                  : sb::lora::launch_dual<32, true>(grid, P, ldp, B, w, Q, m, w, wsplit, d.ldq, d.rows_per_split,
+                                                    partial, upart, d.ldq, st);
+  } else {
+    rc = rh == 16 ? sb::lora::launch_dual<16, false>(grid, P, ldp, B, w, Q, m, w, wsplit, d.ldq, d.rows_per_split,
+                                                     partial, upart, d.ldq, st)
+                  : sb::lora::launch_dual<32, false>(grid, P, ldp, B, w, Q, m, w, wsplit, d.ldq, d.rows_per_split,
+                                                     partial, upart, d.ldq, st);
+  }
+  if (rc) return rc;
+  const int64_t total = w * rh;
+  if (!P) {
+    // u only
+  } else if (d.splits >= 16) {
+    sb::lora::reduce_finalize2_kernel<<<static_cast<unsigned>((total / 4 + 15) / 16), 256, 0, st>>>(
+        partial, d.splits, w, rh, scale_b, transpose_b, db_out, db_dtype);
+    sb::count_launch();
+    if ((rc = sb::check_launch("lora_reduce_finalize2_kernel"))) return rc;
+  } else {
+    sb::lora::reduce_finalize3_kernel<<<static_cast<unsigned>((total / 4 + 255) / 256), 256, 0, st>>>(
+        partial, d.splits, w, rh, scale_b, transpose_b, db_out, db_dtype);
+    sb::count_launch();
+    if ((rc = sb::check_launch("lora_reduce_finalize3_kernel"))) return rc;
+  }
+  const int64_t total4 = d.ldq * (r / 4);
+  sb::lora::dual_u_finalize_kernel<<<static_cast<unsigned>((total4 + 31) / 32), 256, 0, st>>>(
+      upart, d.nblocks, wsplit > 0 ? static_cast<int>(wsplit / sb::lora::kRedCols) : 0, d.ldq, rh, r, m,
+      scale_rows, reinterpret_cast<__half*>(u_rows), ld_rows, scale_t, reinterpret_cast<__half*>(u_t), ldt);
+  sb::count_launch();
+  return sb::check_launch("lora_dual_u_finalize_kernel");
 }
 
 int sb_lora_prepare(const void* a, int a_dtype, const void* b, int b_dtype, int r, int64_t k,

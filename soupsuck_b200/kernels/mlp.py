@@ -33,7 +33,8 @@ from torch.autograd.function import once_differentiable
 from .. import _lib
 from .._spec import HALF, Operand, admit, refuse
 from .nf4 import nested_shape
-from .nf4_gemm import (_factors, _padded_rank, _project, _reduce, _weight_struct, nf4_linear_raw)
+from .nf4_gemm import (_dual, _dual_ok, _factors, _padded_rank, _project, _reduce, _weight_struct,
+                       nf4_linear_raw)
 
 
 # ------------------------------------------------------------------ element-wise SwiGLU
@@ -137,6 +138,18 @@ def _pair_factors(ag, bg, au, bu):
     return pf
 
 
+_SIDE_STREAMS = {}
+
+
+def _side_stream(dev):
+    """One extra stream per device for work that only the optimizer waits for."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _SIDE_STREAMS.get(idx)
+    if st is None:
+        st = _SIDE_STREAMS[idx] = torch.cuda.Stream(device=torch.device("cuda", idx))
+    return st
+
+
 class _FusedMLP(torch.autograd.Function):
     """Forward/backward of the fused MLP.  The gate/up adapters come as a pair or
     not at all (r = 0 for the pair kernel), the down adapter independently."""
@@ -193,28 +206,50 @@ class _FusedMLP(torch.autograd.Function):
         t = g.shape[0]
         dev = g.device
         stream = _lib.stream_of(dev)
-        # down: dact (with its LoRA term) -> (dgate, dup) in one launch
-        ud = ud_t = None
+        # down: dact (with its LoRA term) -> (dgate, dup) in one launch.  The down
+        # adapter's U = s dY.B and dB = s (Z^T.dY)^T come from one pass over dY.
+        ud = ud_t = d_bd = None
         rpd = 0
         if at_d is not None:
             rpd = at_d.shape[1]
-            ud, ud_t = _project(g, bt_d, rpd, s, True, s, True)
+            if _dual_ok(g, zd_t, bt_d, rpd, 0):
+                ud, ud_t, d_bd = _dual(g, zd_t, bt_d, rpd, 0, s, bd_t, s, True, s, True)
+                d_bd = d_bd[:, :r_down]
+            else:
+                ud, ud_t = _project(g, bt_d, rpd, s, True, s, True)
         dgate_up = torch.empty((t, 2 * n), device=dev, dtype=HALF)
         wd = _weight_struct(d_packed, d_state)
         if t:
             _lib.call("sb_nf4_mlp_down_dx", g.data_ptr(), t, ctypes.byref(wd), _lib.ptr(ud), _lib.ptr(at_d),
                       rpd, gate_up.data_ptr(), dgate_up.data_ptr(), stream)
-        d_ad = d_bd = None
+        d_ad = None
+        main = torch.cuda.current_stream(dev)
+        side = None
         if at_d is not None:
-            d_ad = _reduce(ud_t, act, rpd, 1.0, False, ad_t)[:r_down]
-            d_bd = _reduce(zd_t, g, rpd, s, True, bd_t)[:, :r_down]
-        # gate + up: one reduction over both weights, both LoRA terms in one rank-2rp step
-        u_cat = u_cat_t = None
+            if d_bd is None:
+                d_bd = _reduce(zd_t, g, rpd, s, True, bd_t)[:, :r_down]
+            # The down adapter's dA = U_d^T . act only feeds the optimizer: it runs on a
+            # side stream beside the gate/up factor pass below and joins before the
+            # gate/up dX, which would otherwise leave it no SM.
+            side = _side_stream(dev)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                d_ad = _reduce(ud_t, act, rpd, 1.0, False, ad_t)[:r_down]
+            d_ad.record_stream(main)
+        # gate + up: one reduction over both weights, both LoRA terms in one rank-2rp
+        # step; U_cat = s dgate|dup . blockdiag(B_g, B_u) and the two dB blocks come
+        # from one pass over dgate|dup.
+        u_cat = u_cat_t = d_bgu = None
         r2 = 0
         if pair is not None:
             rp = pair[0]
             r2 = 2 * rp
-            u_cat, u_cat_t = _project(dgate_up, bt_bd, r2, s, True, s, True)
+            if _dual_ok(dgate_up, z_t, bt_bd, r2, n):
+                u_cat, u_cat_t, d_bgu = _dual(dgate_up, z_t, bt_bd, r2, n, s, torch.float32, s, True, s, True)
+            else:
+                u_cat, u_cat_t = _project(dgate_up, bt_bd, r2, s, True, s, True)
+        if side is not None:
+            main.wait_stream(side)
         dx = torch.empty((t, h), device=dev, dtype=HALF)
         wg, wu = _weight_struct(g_packed, g_state), _weight_struct(u_packed, u_state)
         if t:
@@ -226,11 +261,15 @@ class _FusedMLP(torch.autograd.Function):
         if pair is not None:
             rp, r_gate, r_up = pair
             d_acat = _reduce(u_cat_t, x2d, r2, 1.0, False, torch.float32)
-            d_bgu = _reduce(z_t, dgate_up, r2, s, True, torch.float32)
             d_ag = d_acat[:r_gate].to(ag_t)
             d_au = d_acat[rp:rp + r_up].to(au_t)
-            d_bg = d_bgu[:n, :r_gate].to(bg_t)
-            d_bu = d_bgu[n:, rp:rp + r_up].to(bu_t)
+            if d_bgu is not None:  # [2N, rp]: each half's rows of its own adapter
+                d_bg = d_bgu[:n, :r_gate].to(bg_t)
+                d_bu = d_bgu[n:, :r_up].to(bu_t)
+            else:
+                d_bgu = _reduce(z_t, dgate_up, r2, s, True, torch.float32)
+                d_bg = d_bgu[:n, :r_gate].to(bg_t)
+                d_bu = d_bgu[n:, rp:rp + r_up].to(bu_t)
         return (dx.reshape(x_shape), None, None, None, d_ag, d_bg, None, None, d_au, d_bu, None, None,
                 d_ad, d_bd)
 

@@ -152,9 +152,18 @@ def _factors(lora_a, lora_b):
     return f
 
 
+# Rows at least this long are projected by the tiled one-pass kernel of
+# sb_lora_dual (u only): [32 x 256] tiles of X staged by cp.async, partials per
+# 256-column block summed in order by a second kernel.
+_WIDE_PROJECT_K = 4096
+
+
 def _project(x2d, w16, rp, scale_rows, want_rows, scale_t, want_t):
     """rows = fp16(scale_rows * X.W^T) [m, rp]; t = fp16(scale_t * X.W^T)^T [rp, m16]."""
     m, k = x2d.shape
+    if m and k >= _WIDE_PROJECT_K and (want_rows or want_t) and _dual_ok(x2d, None, w16, rp, 0):
+        rows, tr, _ = _dual(x2d, None, w16, rp, 0, 1.0, None, scale_rows, want_rows, scale_t, want_t)
+        return rows, tr
     rows = torch.empty((m, rp), dtype=torch.float16, device=x2d.device) if want_rows else None
     ldt = _round16(m)
     tr = torch.empty((rp, ldt), dtype=torch.float16, device=x2d.device) if want_t else None
@@ -162,6 +171,41 @@ def _project(x2d, w16, rp, scale_rows, want_rows, scale_t, want_t):
         _lib.call("sb_lora_project", x2d.data_ptr(), m, k, w16.data_ptr(), rp, float(scale_rows),
                   _lib.ptr(rows), rp, float(scale_t), _lib.ptr(tr), ldt, _lib.stream_of(x2d.device))
     return rows, tr
+
+
+def _dual_ok(q2d, pt, bt, rp, wsplit):
+    w = q2d.shape[1]
+    if wsplit:
+        if rp not in (32, 64) or wsplit % 256 or not 0 < wsplit < w:
+            return False
+    elif rp not in (16, 32):
+        return False
+    if pt is not None and (pt.shape[1] % 16 or pt.data_ptr() % 16):
+        return False
+    return (w % 8 == 0 and q2d.is_contiguous() and bt.is_contiguous() and tuple(bt.shape) == (rp, w)
+            and q2d.data_ptr() % 16 == 0 and bt.data_ptr() % 16 == 0)
+
+
+def _dual(q2d, pt, bt, rp, wsplit, scale_b, b_dtype, scale_rows, want_rows, scale_t, want_t):
+    """One pass over q2d [m, w] for both backward products of a LoRA factor pair:
+    rows / t as ``_project(q2d, bt, rp, ...)`` (U = Q.Bt^T) and
+    db = scale_b * (pt[:, :m] . Q)^T [w, rh] in b_dtype, rh = rp, or rp / 2 for a
+    block-diagonal pair split at column wsplit (each column's rows of its block).
+    pt = None: U only (db is None)."""
+    m, w = q2d.shape
+    rh = rp // 2 if wsplit else rp
+    dev = q2d.device
+    rows = torch.empty((m, rp), dtype=torch.float16, device=dev) if want_rows else None
+    ldt = _round16(m)
+    tr = torch.empty((rp, ldt), dtype=torch.float16, device=dev) if want_t else None
+    db = torch.empty((w, rh), dtype=b_dtype, device=dev) if pt is not None else None
+    nbytes = _lib.query("sb_lora_dual_workspace_bytes", m, w, rp, wsplit)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+    _lib.call("sb_lora_dual", q2d.data_ptr(), m, w, _lib.ptr(pt), 0 if pt is None else pt.shape[1],
+              bt.data_ptr(), rp, wsplit, float(scale_b), 1, _lib.ptr(db),
+              _lib.dtype_code(b_dtype if pt is not None else torch.float32), float(scale_rows), _lib.ptr(rows), rp,
+              float(scale_t), _lib.ptr(tr), ldt, ws.data_ptr(), nbytes, _lib.stream_of(dev))
+    return rows, tr, db
 
 
 def _reduce(pt, q2d, rp, scale, transpose, out_dtype):
@@ -230,8 +274,17 @@ class _NF4LoRALinear(torch.autograd.Function):
             rp, r, s = at16.shape[1], ctx.r, ctx.scaling
             need_a, need_b = ctx.needs_input_grad[3], ctx.needs_input_grad[4]
             need_d = ctx.separate and ctx.needs_input_grad[7]
-            # u = s dY.B: the rank-r factor of the LoRA input gradient (and of dA).
-            u, ut = _project(g, bt16, rp, s, need_x or need_d, s, need_a)
+            # u = s dY.B: the rank-r factor of the LoRA input gradient (and of dA);
+            # with dB = s (Z^T.dY)^T from the same pass over dY when both are wanted.
+            want_u = need_x or need_d or need_a
+            if need_b and want_u and _dual_ok(g, zt, bt16, rp, 0):
+                u, ut, db_full = _dual(g, zt, bt16, rp, 0, s, ctx.b_dtype, s, need_x or need_d, s, need_a)
+                db = db_full[:, :r]
+                need_b = False
+            elif want_u:
+                u, ut = _project(g, bt16, rp, s, need_x or need_d, s, need_a)
+            else:
+                u = ut = None
             if need_x:
                 if ctx.separate:
                     dx = nf4_linear_raw(g, packed, state, transpose=True)
