@@ -24,9 +24,10 @@
 //            memory for bulk tensor stores (6 x 32 KB + 32 KB).
 // Barriers (same offsets in both CTAs):
 //   full[s]      rank 0 only: A bytes of both CTAs (TMA .cta_group::2 loads signal
-//                rank 0's barrier; rank 0's producer expects both halves)
+//                rank 0's barrier; rank 0's producer expects both halves) and 256
+//                decoder-thread arrivals, 128 from each CTA -- one barrier, so the
+//                UMMA issuer waits once per k-step
 //   raw_full[s]  forward, each CTA: its packed codes (plain TMA)
-//   decoded[s]   rank 0 only: 256 decoder-thread arrivals, 128 from each CTA
 //   empty[s]     each CTA: one arrival from rank 0's UMMA commit (multicast to both);
 //                waited on by the producer and, for dX, the decoders (B slot)
 //   acc_full[b]  each CTA: one arrival from rank 0's commit (multicast to both)
@@ -131,6 +132,33 @@ __device__ __forceinline__ void umma_f16_pair_warp(uint32_t d_tmem, uint64_t a_d
       "setp.ne.b32 p, %4, 0;\n\t"
       "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// One k-step of four 256 x 256 x 16 UMMAs and the stage's commit, issued by one
+// elected lane in one sequence: the descriptors of steps 1-3 advance by a_step /
+// b_step in their 16-byte address field, the first UMMA accumulates when
+// `accumulate` is set and the others always.  With the issue spread over separate
+// elect.sync blocks each UMMA cost ~100 cycles of the issuing warp, more than a
+// quarter of a 256 x 256 x 64 k-step's tensor time.
+__device__ __forceinline__ void umma_kstep_pair_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                     uint64_t a_step, uint64_t b_step, uint32_t idesc,
+                                                     uint32_t accumulate, uint64_t* commit_bar) {
+  const uint16_t mask = 3;
+  asm volatile(
+      "{\n\t.reg .pred p, e, t;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 t, 0, 0;\n\t"
+      "add.s64 a1, %1, %5;\n\tadd.s64 a2, a1, %5;\n\tadd.s64 a3, a2, %5;\n\t"
+      "add.s64 b1, %2, %6;\n\tadd.s64 b2, b1, %6;\n\tadd.s64 b3, b2, %6;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a1, b1, %3, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a2, b2, %3, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a3, b3, %3, t;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%7], %8;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "l"(a_step), "l"(b_step),
+      "r"(smem_addr(commit_bar)), "h"(mask)
       : "memory");
 }
 
@@ -601,8 +629,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
   uint8_t* bar_area = staging + C::kStagingBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* raw_full = full + STAGES;  // used by the forward configuration only
-  uint64_t* decoded = raw_full + STAGES;
-  uint64_t* empty = decoded + STAGES;
+  uint64_t* empty = raw_full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
@@ -624,9 +651,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + 2 * 128);  // rank 0's producer + both CTAs' decoder threads
       mbar_init(&raw_full[s], 1);
-      mbar_init(&decoded[s], 2 * 128);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -661,7 +687,6 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
   const int rows_valid = runtime_rows(p);
   // rank 0's barriers, as shared::cluster addresses (stride 8 bytes per barrier)
   const uint32_t leader_full = map_to_rank(smem_addr(full), 0);
-  const uint32_t leader_decoded = map_to_rank(smem_addr(decoded), 0);
   const uint32_t leader_acc_empty = map_to_rank(smem_addr(acc_empty), 0);
 
   if (warp == 0) {
@@ -752,28 +777,28 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           const bool main_step = u.k0 + ls < u.k1;
+          // Both CTAs' A halves landed and both CTAs' decoders arrived.
           if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag, lane)) { ok = false; break; }
-          if (!warp_wait(&decoded[s], ph, kErrWaitDecoded, abort_flag, lane)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + s * C::kStageBytes);
           const uint32_t b_addr = a_addr + C::kABytes;
           if (main_step) {
-#pragma unroll
-            for (int k16 = 0; k16 < kBK / 16; ++k16) {
-              const uint64_t bdesc = C::kBMN
-                  ? smem_desc(b_addr + k16 * 16 * 128, 64 * 128, 1024, kSwizzle128B)
-                  : smem_desc(b_addr + k16 * 32, 16, 1024, kSwizzle128B);
-              const uint64_t adesc = smem_desc(a_addr + k16 * 32, 16, 1024, kSwizzle128B);
-              umma_f16_pair_warp(acc, adesc, bdesc, kIdesc, (ls > 0 || k16 > 0) ? 1u : 0u);
-            }
+            static_assert(kBK == 64, "four K=16 UMMAs per k-step");
+            const uint64_t bdesc = C::kBMN ? smem_desc(b_addr, 64 * 128, 1024, kSwizzle128B)
+                                           : smem_desc(b_addr, 16, 1024, kSwizzle128B);
+            const uint64_t adesc = smem_desc(a_addr, 16, 1024, kSwizzle128B);
+            // Address-field steps (16-byte units): 32 bytes of K for a K-major operand,
+            // a 16-row x 128-byte block for the MN-major dX operand.
+            umma_kstep_pair_warp(acc, adesc, bdesc, 32 >> 4, C::kBMN ? (16 * 128) >> 4 : 32 >> 4, kIdesc,
+                                 ls > 0 ? 1u : 0u, &empty[s]);
           } else {
             for (int k16 = 0; k16 < p.lora_r / 16; ++k16) {
               const uint64_t bdesc = smem_desc(b_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
               const uint64_t adesc = smem_desc(a_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
               umma_f16_pair_warp(acc, adesc, bdesc, kIdescLora, 1u);
             }
+            umma_commit_both_warp(&empty[s]);
           }
-          umma_commit_both_warp(&empty[s]);
         }
         if (ok) umma_commit_both_warp(&acc_full[buf]);
         ++tl;
@@ -800,7 +825,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
     // ------------------------------------------------------------ NF4 decoders (both CTAs)
     // Group g decodes the k-steps whose running index has parity g; thread gtid
     // decodes one (row, 64-block) of this CTA's 128-row half per step and
-    // arrives on rank 0's decoded barrier.  The block's 32 packed bytes, its
+    // arrives on rank 0's full barrier.  The block's 32 packed bytes, its
     // qabs byte and absmax2 value are loaded for the group's next step while the
     // current one decodes; the B slot is reused once empty[s] shows the UMMA
     // that read it has completed.
@@ -928,7 +953,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
           }
         }
         fence_proxy_async_smem();
-        mbar_arrive_cluster(leader_decoded + 8u * s);
+        mbar_arrive_cluster(leader_full + 8u * s);
       }
     }
   }
