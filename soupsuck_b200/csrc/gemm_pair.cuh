@@ -15,10 +15,12 @@
 // Per stage and CTA: A 128 x 64 fp16 (16 KB, SW128) and decoded B 128 x 64 fp16
 // (16 KB, SW128; K-major for the forward, two MN-major 64-column panels for dX).
 // Measured configurations (B200, Qwen2.5 layer shapes):
-//   forward: the producer also TMA-loads each step's packed codes (4 KB) into the
-//            stage (raw_full[s]); whole tiles run 4 stages and stage the output
-//            for bulk tensor stores (4 x 36 KB + 32 KB), stream-K runs 6 stages
-//            and stores fp16 rows directly (6 x 36 KB);
+//   forward: a second producer thread TMA-loads each step's packed codes (4 KB)
+//            into a ring of 8 slots of their own (raw_full / raw_empty), so the
+//            codes wait in shared memory for their B slot; whole tiles run 4
+//            operand stages and stage the output for bulk tensor stores
+//            (4 x 32 KB + 32 KB codes + 32-48 KB staging), stream-K runs 6 stages
+//            and stores fp16 rows directly (6 x 32 KB + 32 KB);
 //   dX:      the decoders load their packed codes straight from global memory one
 //            owned step ahead, and the epilogue stages 32 x 64 boxes in shared
 //            memory for bulk tensor stores (6 x 32 KB + 32 KB).
@@ -27,7 +29,8 @@
 //                rank 0's barrier; rank 0's producer expects both halves) and 256
 //                decoder-thread arrivals, 128 from each CTA -- one barrier, so the
 //                UMMA issuer waits once per k-step
-//   raw_full[s]  forward, each CTA: its packed codes (plain TMA)
+//   raw_full[r]  forward, each CTA: code-ring slot r loaded (plain TMA)
+//   raw_empty[r] forward, each CTA: slot r read by its 128 decoder threads
 //   empty[s]     each CTA: one arrival from rank 0's UMMA commit (multicast to both);
 //                waited on by the producer and, for dX, the decoders (B slot)
 //   acc_full[b]  each CTA: one arrival from rank 0's commit (multicast to both)
@@ -217,8 +220,14 @@ struct PairCfg {
   // row stores (gate projection, T = 3300) -- the 6-stage stream-K forward has
   // no room for the staging and stores directly.
   static constexpr bool kStoreStage = !kRawTma || STAGES == 4;
+  // The forward's packed codes (4 KB per k-step) have their own ring, twice as
+  // deep as the operand stages, filled by a second producer thread: a k-step's
+  // codes are in shared memory before its B slot frees, so the decode follows the
+  // UMMA that released the slot directly instead of waiting for a TMA load issued
+  // after it.
   static constexpr int kRawBytes = kRawTma ? kHalfN * kBK / 2 : 0;   // 4 KB
-  static constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;
+  static constexpr int kRawStages = kRawTma ? 8 : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
   static constexpr int kThreads = 512;
   static constexpr int kBarrierBytes = 1024 + 1024;        // barriers + the code2 table
@@ -229,7 +238,8 @@ struct PairCfg {
   // SwiGLU backward.
   static constexpr int kBoxes = EMODE == kSwiGLUFwd ? 3 : (EMODE == kSwiGLUBwd ? 4 : 2);
   static constexpr int kStagingBytes = kStoreStage ? 4 * kBoxes * kStoreBoxBytes : 0;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + kStagingBytes + kBarrierBytes + 1024;
+  static constexpr int kSmemBytes =
+      STAGES * kStageBytes + kRawStages * kRawBytes + kStagingBytes + kBarrierBytes + 1024;
   static_assert(STAGES % 2 == 0, "two decoder groups alternate stages: each stage keeps one group");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kSmemBytes > 232448 / 2, "one CTA per SM keeps TMEM allocation uncontended");
@@ -625,11 +635,13 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
                 "weight selection: 1 = gate/up forward (whole tiles), 2 = two-weight dX");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + STAGES * C::kStageBytes;
+  uint8_t* raw_ring = smem + STAGES * C::kStageBytes;  // forward: kRawStages x 4 KB of packed codes
+  uint8_t* staging = raw_ring + C::kRawStages * C::kRawBytes;
   uint8_t* bar_area = staging + C::kStagingBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
-  uint64_t* raw_full = full + STAGES;  // used by the forward configuration only
-  uint64_t* empty = raw_full + STAGES;
+  uint64_t* raw_full = full + STAGES;  // forward only: the code ring's slots
+  uint64_t* raw_empty = raw_full + 8;
+  uint64_t* empty = raw_empty + 8;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
@@ -652,8 +664,11 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1 + 2 * 128);  // rank 0's producer + both CTAs' decoder threads
-      mbar_init(&raw_full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < C::kRawStages; ++r) {
+      mbar_init(&raw_full[r], 1);
+      mbar_init(&raw_empty[r], 128);  // the decoder group of the slot's k-step, this CTA
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -693,9 +708,6 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
-      // Gate/up pairing: the rank-1 CTA loads the second weight's packed codes.
-      const CUtensorMap* bmap = (WSEL == 1 && rank == 1) ? &tmB2 : &tmB;
-      if (C::kRawTma) tma_prefetch_desc(bmap);
       if (has_lora) {
         tma_prefetch_desc(&tmLA);
         tma_prefetch_desc(&tmLB);
@@ -711,8 +723,8 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
         const int arow = m0 + static_cast<int>(rank) * kTileRows;
         // A gate/up tile covers output columns nt*128.. of both weights; its LoRA B
         // rows come from the [2N, r] stack of both weights' factors.
-        const int brow = WSEL == 1 ? nt * kHalfN : nt * kTileN + static_cast<int>(rank) * kHalfN;
-        const int lbrow = WSEL == 1 ? static_cast<int>(rank) * p.N + nt * kHalfN : brow;
+        const int lbrow = WSEL == 1 ? static_cast<int>(rank) * p.N + nt * kHalfN
+                                    : nt * kTileN + static_cast<int>(rank) * kHalfN;
         const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
         for (int ls = 0; ls < nsteps; ++ls, ++it) {
           const int s = it % STAGES;
@@ -724,15 +736,10 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
           if (step < u.k1) {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kABytes);
             tma_load_2d_pair(a_s, &tmA, leader_full + 8u * s, step * kBK, arow);
-            if constexpr (C::kRawTma) {
-              mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
-              tma_load_2d(b_s + C::kBBytes, bmap, &raw_full[s], step * (kBK / 2), brow);
-            }
           } else {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * (kTileRows + kHalfN) * p.lora_r * 2);
             tma_load_2d_pair(a_s, &tmLA, leader_full + 8u * s, 0, arow);
             tma_load_2d_pair(b_s, &tmLB, leader_full + 8u * s, 0, lbrow);
-            if constexpr (C::kRawTma) mbar_arrive(&raw_full[s]);  // nothing to decode
           }
         }
       }
@@ -747,10 +754,55 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
       if (!clean) {
         const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0;
         for (uint32_t j = first; j < it; ++j) {
-          if (C::kRawTma) mbar_wait(&raw_full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
           if (leader) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, kErrWaitDrain, &drain_abort);
         }
       }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ packed-code producer (forward, both CTAs)
+    // Fills the code ring kRawStages k-steps ahead of the decoders; a slot is
+    // refilled once its decoder group has read it (raw_empty).  Gate/up pairing:
+    // the rank-1 CTA loads the second weight's codes.
+    if constexpr (C::kRawTma) {
+     if (lane == 0) {
+      const CUtensorMap* bmap = (WSEL == 1 && rank == 1) ? &tmB2 : &tmB;
+      tma_prefetch_desc(bmap);
+      uint32_t it = 0;
+      bool ok = true;
+      UnitIter iter(p, num_tiles, pair_id, pairs);
+      Unit u;
+      while (ok && iter.next(u)) {
+        const int mt = tile_m(p, u.tile), nt = tile_n(p, u.tile);
+        if (mt * kTileM >= rows_valid) continue;
+        const int brow = WSEL == 1 ? nt * kHalfN : nt * kTileN + static_cast<int>(rank) * kHalfN;
+        const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
+        for (int ls = 0; ls < nsteps; ++ls, ++it) {
+          const int r = static_cast<int>(it % C::kRawStages);
+          const uint32_t rph = (it / C::kRawStages) & 1;
+          if (!mbar_wait(&raw_empty[r], rph ^ 1, kErrWaitEmpty, abort_flag)) { ok = false; break; }
+          const int step = u.k0 + ls;
+          if (step < u.k1) {
+            mbar_arrive_expect_tx(&raw_full[r], C::kRawBytes);
+            tma_load_2d(raw_ring + r * C::kRawBytes, bmap, &raw_full[r], step * (kBK / 2), brow);
+          } else {
+            mbar_arrive(&raw_full[r]);  // the LoRA step: nothing to decode
+          }
+        }
+      }
+      // Tail: every slot filled above read by its decoders before exit; after an
+      // abort, wait (bounded once in total) for the loads still in flight.
+      volatile int drain_abort = 0;
+      bool clean = ok && !*abort_flag;
+      for (uint32_t j = it; clean && j < it + C::kRawStages; ++j) {
+        clean = mbar_wait(&raw_empty[j % C::kRawStages], ((j / C::kRawStages) & 1) ^ 1, kErrWaitDrain, abort_flag);
+      }
+      if (!clean) {
+        const uint32_t first = it > static_cast<uint32_t>(C::kRawStages) ? it - C::kRawStages : 0;
+        for (uint32_t j = first; j < it; ++j) {
+          mbar_wait(&raw_full[j % C::kRawStages], (j / C::kRawStages) & 1, kErrWaitDrain, &drain_abort);
+        }
+      }
+     }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (rank 0)
@@ -923,10 +975,26 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
           a2_next = __ldg(wv.absmax2 + (nb >> 8));
           second_next = in_second(step + 2);
         }
-        // Forward: raw_full[s] (the producer loaded the packed codes after empty[s]).
-        // dX: empty[s] (the UMMA that read this B slot has completed).
-        if (C::kRawTma ? !mbar_wait(&raw_full[s], ph, kErrWaitFull, abort_flag)
-                       : !mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
+        // Forward: the step's packed codes (raw_full), read into registers; the slot
+        // is released after the decode has used them.  Every step: the B slot free
+        // again (empty[s]: the UMMA that read it has completed), which also orders
+        // this arrival on full[s] after the slot's previous phase.
+        uint4 rp0 = make_uint4(0, 0, 0, 0), rp1 = make_uint4(0, 0, 0, 0);
+        const int r = C::kRawTma ? static_cast<int>(it % (C::kRawTma ? C::kRawStages : 1)) : 0;
+        if constexpr (C::kRawTma) {
+          if (!mbar_wait(&raw_full[r], (it / C::kRawStages) & 1, kErrWaitFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (valid) {
+            // Packed rows are 32 B, TMA-swizzled in 32 B spans: chunk ^= (row >> 2) & 1.
+            const uint8_t* raw_s = raw_ring + r * C::kRawBytes + gtid * 32;
+            const uint32_t x = static_cast<uint32_t>((gtid >> 2) & 1);
+            rp0 = *reinterpret_cast<const uint4*>(raw_s + (x << 4));
+            rp1 = *reinterpret_cast<const uint4*>(raw_s + ((x ^ 1u) << 4));
+          }
+        }
+        if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
           ok = false;
           break;
         }
@@ -938,11 +1006,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
             scale = __fadd_rn(__fmul_rn(code, a2_cur), second_cur ? second_w.off : own_w.off);
           }
           if constexpr (C::kRawTma) {
-            // Packed rows are 32 B, TMA-swizzled in 32 B spans: chunk ^= (row >> 2) & 1.
-            const uint8_t* raw_s = b_s + C::kBBytes;
-            const uint32_t x = static_cast<uint32_t>((gtid >> 2) & 1);
-            nf4_decode_row(raw_s + gtid * 32 + (x << 4), raw_s + gtid * 32 + ((x ^ 1u) << 4), b_s + gtid * 128,
-                           gtid, scale, valid);
+            nf4_decode_words(rp0, rp1, b_s + gtid * 128, gtid, scale, valid);
           } else if constexpr (BMODE == kNF4Fwd) {
             nf4_decode_words(w0, w1, b_s + gtid * 128, gtid, scale, valid);
           } else {
@@ -952,7 +1016,10 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
             nf4_decode_words_flip(w0, w1, b_s + j * (kBK * 128) + r * 128, r, scale, valid, 4u * j);
           }
         }
+        // The decoded B (generic writes) before the UMMA reads it, and the code slot's
+        // generic reads before the next TMA write into it (both async proxy).
         fence_proxy_async_smem();
+        if constexpr (C::kRawTma) mbar_arrive(&raw_empty[r]);
         mbar_arrive_cluster(leader_full + 8u * s);
       }
     }
