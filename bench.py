@@ -218,7 +218,7 @@ def layer_step(torch, layer, inp, streams=None):
     from synthetic upstream gradients of q, k, v and the layer output.  With
     ``streams`` (two side streams) the projections that do not depend on each
     other run concurrently: o_proj (its input is a layer input) on one side
-    stream, k/v beside q on the other.  Autograd runs every backward node on the
+    stream, q/k/v on the other.  Autograd runs every backward node on the
     stream of its forward, so the backward overlaps the same way; all streams are
     joined before returning."""
     from soupsuck_b200.kernels import add_rms_norm, nf4_lora_linear, nf4_swiglu_mlp
@@ -249,8 +249,7 @@ def layer_step(torch, layer, inp, streams=None):
     s1, y1 = add_rms_norm(inp["residual"], inp["mlp_prev"], layer["gamma_in"], EPS)
     sa.wait_stream(main)
     with torch.cuda.stream(sa):
-        k, v = proj("k", y1), proj("v", y1)
-    q = proj("q", y1)
+        q, k, v = proj("q", y1), proj("k", y1), proj("v", y1)
     main.wait_stream(sb)
     s2, y2 = add_rms_norm(s1, o, layer["gamma_post"], EPS)
     out = s2 + mlp(y2)
@@ -1096,7 +1095,7 @@ def main():
                    "parallelism": f"dp{world}" + (" + LoRA-grad NCCL all-reduce" if world > 1 else ""),
                    "l2": "flushed (256 MiB write) before every timed step, outside the events",
                    "cuda_graph": used_graph,
-                   "streams": "o and k/v on two side streams" if streams else "one stream"},
+                   "streams": "o and q/k/v on two side streams" if streams else "one stream"},
         "pct_peak": 100.0 * value / (peak_burst * world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": 1000 * e2e_sec,
