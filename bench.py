@@ -814,7 +814,7 @@ def run_stack(args, torch):
             "scaling": "strong", "dtype": "f16", "data": "synthetic (seeded lengths U[64,512], 4 rows x 64 batches)",
             "pct_peak": 100 * flops / sec / 1e12 / (peak_sust * world),
             "peak": "sustained bf16 (MEASURED_PEAKS.json)",
-            "config": {"workload": "configs[2]: 28 layers x 7 NF4+LoRA(r=16) projections + 2 add-RMSNorm, fwd+bwd",
+            "config": {"workload": "configs[2]: 28 layers x 7 NF4+LoRA(r=16) projections (MLP as the fused gate/up+SwiGLU -> down chain) + 2 add-RMSNorm, fwd+bwd",
                        "batches": STACK_BATCHES, "tokens": tokens, "padded_rows": padded,
                        "bucket_rows": STACK_BUCKET, "cuda_graph": bool(graphs), "graphs": len(graphs),
                        "streams": "k/v on a side stream" if kv_stream is not None else "one stream",
