@@ -229,7 +229,9 @@ struct PairCfg {
   static constexpr int kRawStages = kRawTma ? 8 : 0;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
-  static constexpr int kThreads = 512;
+  // Decoder groups of four warps; k-step i is decoded by group i % kDecGroups.
+  static constexpr int kDecGroups = 3;
+  static constexpr int kThreads = (8 + 4 * kDecGroups) * 32;
   static constexpr int kBarrierBytes = 1024 + 1024;        // barriers + the code2 table
   // Epilogue staging: per epilogue warp two 32-row x 64-column fp16 boxes (SW128);
   // three for the SwiGLU forward, whose panels go out as gate, up and activation.
@@ -240,7 +242,6 @@ struct PairCfg {
   static constexpr int kStagingBytes = kStoreStage ? 4 * kBoxes * kStoreBoxBytes : 0;
   static constexpr int kSmemBytes =
       STAGES * kStageBytes + kRawStages * kRawBytes + kStagingBytes + kBarrierBytes + 1024;
-  static_assert(STAGES % 2 == 0, "two decoder groups alternate stages: each stage keeps one group");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kSmemBytes > 232448 / 2, "one CTA per SM keeps TMEM allocation uncontended");
   static_assert(BMODE == kNF4Fwd || BMODE == kNF4Dx, "NF4 operand modes only");
@@ -935,7 +936,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
       const int nt = tile_n(p, u.tile);
       const int n0 = WSEL == 1 ? nt * kHalfN : nt * kTileN + static_cast<int>(rank) * kHalfN;
       const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
-      const int first = u.k0 + ((static_cast<int>(it & 1) == group) ? 0 : 1);
+      const int first = u.k0 + (group - static_cast<int>(it % C::kDecGroups) + C::kDecGroups) % C::kDecGroups;
       int64_t nb = first < u.k1 ? block_of(n0, first) : -1;
       uint4 w0_next = make_uint4(0, 0, 0, 0), w1_next = make_uint4(0, 0, 0, 0);
       uint32_t q_next = 0u;
@@ -953,7 +954,7 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
         second_next = in_second(first);
       }
       for (int ls = 0; ls < nsteps; ++ls, ++it) {
-        if (static_cast<int>(it & 1) != group) continue;
+        if (static_cast<int>(it % C::kDecGroups) != group) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         const int step = u.k0 + ls;
@@ -963,17 +964,17 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
         const float a2_cur = a2_next;
         const bool second_cur = second_next;
         const bool valid = main_step && block_of(n0, step) >= 0;
-        nb = step + 2 < u.k1 ? block_of(n0, step + 2) : -1;
+        nb = step + C::kDecGroups < u.k1 ? block_of(n0, step + C::kDecGroups) : -1;
         if (nb >= 0) {
-          const WView& wv = view_of(step + 2);
+          const WView& wv = view_of(step + C::kDecGroups);
           if constexpr (!C::kRawTma) {
-            const uint4* src = reinterpret_cast<const uint4*>(wv.packed + bytes_of(n0, step + 2));
+            const uint4* src = reinterpret_cast<const uint4*>(wv.packed + bytes_of(n0, step + C::kDecGroups));
             w0_next = ld_stream16(src);
             w1_next = ld_stream16(src + 1);
           }
           q_next = __ldg(wv.qabs + nb);
           a2_next = __ldg(wv.absmax2 + (nb >> 8));
-          second_next = in_second(step + 2);
+          second_next = in_second(step + C::kDecGroups);
         }
         // Forward: the step's packed codes (raw_full), read into registers; the slot
         // is released after the decode has used them.  Every step: the B slot free
