@@ -230,7 +230,9 @@ struct PairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
   // Decoder groups of four warps; k-step i is decoded by group i % kDecGroups.
-  static constexpr int kDecGroups = 3;
+  // Three groups measured faster except in the 6-stage stream-K forward, whose
+  // registers at 640 threads spill (down forward 117 -> 123 us): two there.
+  static constexpr int kDecGroups = (BMODE == kNF4Fwd && STAGES == 6) ? 2 : 3;
   static constexpr int kThreads = (8 + 4 * kDecGroups) * 32;
   static constexpr int kBarrierBytes = 1024 + 1024;        // barriers + the code2 table
   // Epilogue staging: per epilogue warp two 32-row x 64-column fp16 boxes (SW128);
