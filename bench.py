@@ -92,8 +92,8 @@ def pass_bytes(m):
 # pass, from a separate ncu capture of `bench.py --kernel-case gemm_pass --warmup 1
 # --steps 1` (-k regex:pair_kernel -s 12 -c 12; ncu cannot run inside the timed
 # bench).  A static figure: it is reported as such and describes the kernels of
-# the capture it came from (626.0 MB read + 226.8 MB written).
-PASS_TRAFFIC_NCU = {3300: 852767232}
+# the capture it came from (624.9 MB read + 227.2 MB written).
+PASS_TRAFFIC_NCU = {3300: 852130560}
 
 
 def static_pass_traffic(m):
