@@ -123,8 +123,9 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la,
 
 // ----------------------------------------------------------------- 2-SM pair launch
 constexpr int kPairStages = 6;         // dX, and the stream-K forward
-constexpr int kPairFwdTileStages = 4;  // whole-tile forward (leaves room for store staging)
-constexpr int kPairMlpBwdStages = 4;   // down dX + SwiGLU derivatives (room for the gate/up box sets)
+constexpr int kPairFwdTileStages = 5;  // whole-tile forward (leaves room for store staging; 4 code slots)
+constexpr int kPairMlpFwdStages = 4;   // gate/up + SwiGLU forward (three staging boxes per warp; 5 measured slower)
+constexpr int kPairMlpBwdStages = 4;   // down dX + SwiGLU derivatives (gate/up box sets; 5 measured slower)
 
 template <int BMODE, int EMODE, int STAGES, bool SK, int WSEL = 0>
 inline int configure_pair(const char* name) {
@@ -444,7 +445,7 @@ inline int mlp_gate_up(const uint16_t* x, int64_t m, const sb_nf4_weight& wg, co
   const int64_t tiles = m_tiles * n_tiles;
   const int slots = pair_slots();
   const int grid = 2 * static_cast<int>(tiles < slots ? tiles : slots);
-  return launch_pair_sk<kNF4Fwd, kSwiGLUFwd, kPairFwdTileStages, false, 1>(ta, tb, tla, tlb, ty, p, grid, stream,
+  return launch_pair_sk<kNF4Fwd, kSwiGLUFwd, kPairMlpFwdStages, false, 1>(ta, tb, tla, tlb, ty, p, grid, stream,
                                                                             "nf4_mlp_gate_up", &tb2, &ty2);
 }
 

@@ -219,14 +219,14 @@ struct PairCfg {
   // 4-stage whole-tile configuration, where it measured 12 % faster than direct
   // row stores (gate projection, T = 3300) -- the 6-stage stream-K forward has
   // no room for the staging and stores directly.
-  static constexpr bool kStoreStage = !kRawTma || STAGES == 4;
+  static constexpr bool kStoreStage = !kRawTma || STAGES <= 5;
   // The forward's packed codes (4 KB per k-step) have their own ring, twice as
   // deep as the operand stages, filled by a second producer thread: a k-step's
   // codes are in shared memory before its B slot frees, so the decode follows the
   // UMMA that released the slot directly instead of waiting for a TMA load issued
   // after it.
   static constexpr int kRawBytes = kRawTma ? kHalfN * kBK / 2 : 0;   // 4 KB
-  static constexpr int kRawStages = kRawTma ? 8 : 0;
+  static constexpr int kRawStages = kRawTma ? (STAGES == 5 ? 4 : 8) : 0;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * kTileN;             // two accumulators of 256 columns
   // Decoder groups of four warps; k-step i is decoded by group i % kDecGroups.
