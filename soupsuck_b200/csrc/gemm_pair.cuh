@@ -144,24 +144,29 @@ __device__ __forceinline__ void umma_f16_pair_warp(uint32_t d_tmem, uint64_t a_d
 // `accumulate` is set and the others always.  With the issue spread over separate
 // elect.sync blocks each UMMA cost ~100 cycles of the issuing warp, more than a
 // quarter of a 256 x 256 x 64 k-step's tensor time.
-__device__ __forceinline__ void umma_kstep_pair_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                                     uint64_t a_step, uint64_t b_step, uint32_t idesc,
-                                                     uint32_t accumulate, uint64_t* commit_bar) {
+__device__ __forceinline__ void umma_kstep_pair_warp(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                                     uint32_t b_hi, uint32_t a_step, uint32_t b_step, uint32_t idesc,
+                                                     uint32_t accumulate, uint32_t commit_bar) {
+  // Descriptors as 32-bit halves: the address field lives in the low word, so
+  // the steps are 32-bit adds and the high words are loop constants.
   const uint16_t mask = 3;
   asm volatile(
-      "{\n\t.reg .pred p, e, t;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "{\n\t.reg .pred p, e, t;\n\t.reg .b32 x1, x2, x3, y1, y2, y3;\n\t"
+      ".reg .b64 a0, a1, a2, a3, b0, b1, b2, b3;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
       "setp.eq.b32 t, 0, 0;\n\t"
-      "add.s64 a1, %1, %5;\n\tadd.s64 a2, a1, %5;\n\tadd.s64 a3, a2, %5;\n\t"
-      "add.s64 b1, %2, %6;\n\tadd.s64 b2, b1, %6;\n\tadd.s64 b3, b2, %6;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a1, b1, %3, t;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a2, b2, %3, t;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a3, b3, %3, t;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%7], %8;\n\t}"
-      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "l"(a_step), "l"(b_step),
-      "r"(smem_addr(commit_bar)), "h"(mask)
+      "add.u32 x1, %1, %6;\n\tadd.u32 x2, x1, %6;\n\tadd.u32 x3, x2, %6;\n\t"
+      "add.u32 y1, %3, %7;\n\tadd.u32 y2, y1, %7;\n\tadd.u32 y3, y2, %7;\n\t"
+      "mov.b64 a0, {%1, %2};\n\tmov.b64 a1, {x1, %2};\n\tmov.b64 a2, {x2, %2};\n\tmov.b64 a3, {x3, %2};\n\t"
+      "mov.b64 b0, {%3, %4};\n\tmov.b64 b1, {y1, %4};\n\tmov.b64 b2, {y2, %4};\n\tmov.b64 b3, {y3, %4};\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a0, b0, %8, p;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a1, b1, %8, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a2, b2, %8, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a3, b3, %8, t;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%9], %10;\n\t}"
+      ::"r"(d_tmem), "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(accumulate), "r"(a_step), "r"(b_step),
+      "r"(idesc), "r"(commit_bar), "h"(mask)
       : "memory");
 }
 
@@ -816,7 +821,17 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
       constexpr uint32_t kIdescLora = idesc_f16_f32(kTileM, kTileN, 0, 0);
       const uint32_t lora_layout = p.lora_r == 16 ? kSwizzle32B : (p.lora_r == 32 ? kSwizzle64B : kSwizzle128B);
       const uint32_t lora_pitch = static_cast<uint32_t>(p.lora_r) * 2;
-      uint32_t it = 0, tl = 0;
+      // Stage and phase of the next k-step (the step count modulo STAGES and the
+      // parity of its quotient), advanced per step; stage s's descriptors are the
+      // stage-0 ones plus s stages in the address field.
+      uint32_t st = 0, ph = 0, tl = 0;
+      static_assert(kBK == 64, "four K=16 UMMAs per k-step");
+      const uint64_t ad0 = smem_desc(smem_addr(smem), 16, 1024, kSwizzle128B);
+      const uint64_t bd0 = C::kBMN ? smem_desc(smem_addr(smem) + C::kABytes, 64 * 128, 1024, kSwizzle128B)
+                                   : smem_desc(smem_addr(smem) + C::kABytes, 16, 1024, kSwizzle128B);
+      const uint32_t a_lo0 = static_cast<uint32_t>(ad0), a_hi = static_cast<uint32_t>(ad0 >> 32);
+      const uint32_t b_lo0 = static_cast<uint32_t>(bd0), b_hi = static_cast<uint32_t>(bd0 >> 32);
+      const uint32_t empty_addr = smem_addr(empty);
       bool ok = true;
       UnitIter iter(p, num_tiles, pair_id, pairs);
       Unit u;
@@ -827,32 +842,33 @@ __global__ void __launch_bounds__(PairCfg<BMODE, STAGES, EMODE>::kThreads, 1)
         if (!warp_wait(&acc_empty[buf], aph ^ 1, kErrWaitAccEmpty, abort_flag, lane)) { ok = false; break; }
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * kTileN;
-        const int nsteps = (u.k1 - u.k0) + ((has_lora && u.k1 == p.k_blocks) ? 1 : 0);
-        for (int ls = 0; ls < nsteps; ++ls, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          const bool main_step = u.k0 + ls < u.k1;
+        const int nmain = u.k1 - u.k0;
+        const bool lora_step = has_lora && u.k1 == p.k_blocks;
+        for (int ls = 0; ls < nmain; ++ls) {
           // Both CTAs' A halves landed and both CTAs' decoders arrived.
-          if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag, lane)) { ok = false; break; }
+          if (!warp_wait(full + st, ph, kErrWaitFull, abort_flag, lane)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_addr(smem + s * C::kStageBytes);
-          const uint32_t b_addr = a_addr + C::kABytes;
-          if (main_step) {
-            static_assert(kBK == 64, "four K=16 UMMAs per k-step");
-            const uint64_t bdesc = C::kBMN ? smem_desc(b_addr, 64 * 128, 1024, kSwizzle128B)
-                                           : smem_desc(b_addr, 16, 1024, kSwizzle128B);
-            const uint64_t adesc = smem_desc(a_addr, 16, 1024, kSwizzle128B);
-            // Address-field steps (16-byte units): 32 bytes of K for a K-major operand,
-            // a 16-row x 128-byte block for the MN-major dX operand.
-            umma_kstep_pair_warp(acc, adesc, bdesc, 32 >> 4, C::kBMN ? (16 * 128) >> 4 : 32 >> 4, kIdesc,
-                                 ls > 0 ? 1u : 0u, &empty[s]);
+          const uint32_t off = st * (C::kStageBytes >> 4);
+          // Address-field steps (16-byte units): 32 bytes of K for a K-major operand,
+          // a 16-row x 128-byte block for the MN-major dX operand.
+          umma_kstep_pair_warp(acc, a_lo0 + off, a_hi, b_lo0 + off, b_hi, 32 >> 4,
+                               C::kBMN ? (16 * 128) >> 4 : 32 >> 4, kIdesc, ls > 0 ? 1u : 0u, empty_addr + 8u * st);
+          if (++st == static_cast<uint32_t>(STAGES)) { st = 0; ph ^= 1u; }
+        }
+        if (ok && lora_step) {
+          if (!warp_wait(full + st, ph, kErrWaitFull, abort_flag, lane)) {
+            ok = false;
           } else {
+            tc_fence_after();
+            const uint32_t a_addr = smem_addr(smem + st * C::kStageBytes);
+            const uint32_t b_addr = a_addr + C::kABytes;
             for (int k16 = 0; k16 < p.lora_r / 16; ++k16) {
               const uint64_t bdesc = smem_desc(b_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
               const uint64_t adesc = smem_desc(a_addr + k16 * 32, 16, 8 * lora_pitch, lora_layout);
               umma_f16_pair_warp(acc, adesc, bdesc, kIdescLora, 1u);
             }
-            umma_commit_both_warp(&empty[s]);
+            umma_commit_both_warp(&empty[st]);
+            if (++st == static_cast<uint32_t>(STAGES)) { st = 0; ph ^= 1u; }
           }
         }
         if (ok) umma_commit_both_warp(&acc_full[buf]);
