@@ -1003,9 +1003,10 @@ def main():
 
     # ---- end-to-end through the public API with host buffers: every step copies
     # its inputs from pinned host memory and reads the layer-input gradient back.
-    # With graphs the steps alternate between the two input sets, and the copy of
-    # step i+1's inputs (on a copy stream) overlaps step i; a set is overwritten
-    # only after the step that read it has finished.
+    # With graphs the steps alternate between the two input sets: the copy of step
+    # i+1's inputs (on a copy stream) and the read-back of step i-1's result (on a
+    # second copy stream, the other PCIe direction) overlap step i; a set's inputs
+    # and result buffer are reused only after its previous read-back has finished.
     host = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in dev_in.items()}
     for k in host:
         host[k].copy_(dev_in[k].detach())
@@ -1013,6 +1014,7 @@ def main():
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = out_host[0].numel() * out_host[0].element_size()
     copy_stream = torch.cuda.Stream(device)
+    back_stream = torch.cuda.Stream(device)
     e2e_steps = max(3, min(args.steps, 10))
 
     def e2e_run(n):
@@ -1026,10 +1028,12 @@ def main():
             return
         done = [None, None]
         copy_stream.wait_stream(stream)
+        back_stream.wait_stream(stream)
         for i in range(n):
             j = i % len(sets)
             if done[j] is not None:
                 copy_stream.wait_event(done[j])
+                stream.wait_event(done[j])
             with torch.cuda.stream(copy_stream), torch.no_grad():
                 for k, hv in host.items():
                     sets[j][k].copy_(hv, non_blocking=True)
@@ -1037,10 +1041,15 @@ def main():
             copied.record(copy_stream)
             stream.wait_event(copied)
             graphs[j].replay()
-            out_host[j].copy_(graph_out[j], non_blocking=True)
+            computed = torch.cuda.Event()
+            computed.record(stream)
+            back_stream.wait_event(computed)
+            with torch.cuda.stream(back_stream):
+                out_host[j].copy_(graph_out[j], non_blocking=True)
             done[j] = torch.cuda.Event()
-            done[j].record(stream)
+            done[j].record(back_stream)
         stream.wait_stream(copy_stream)
+        stream.wait_stream(back_stream)
 
     e2e_run(2)
     torch.cuda.synchronize()
@@ -1099,7 +1108,7 @@ def main():
         "pct_peak": 100.0 * value / (peak_burst * world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": 1000 * e2e_sec,
-                "pipelining": "next step's host->device copy overlaps the current step (two input sets)"
+                "pipelining": "next step's host->device copy and the previous step's device->host read-back (one copy stream each) overlap the current step (two input sets)"
                               if used_graph else "none"},
         "gpu_launches": int(launches_per_step) * args.steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_burst, "unit": "TFLOP/s",
