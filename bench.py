@@ -573,10 +573,11 @@ def run_sweep(args, torch):
             for c in calls:
                 c()
         torch.cuda.synchronize()
-        # Single GPU: the pass is replayed from a CUDA graph, so host launch overhead
-        # (which exceeds the kernels' own time at M <= 16) stays out of the timing.
+        # The pass is replayed from a CUDA graph (with its NCCL collectives on N
+        # GPUs), so host launch overhead -- which exceeds the kernels' own time at
+        # M <= 16 -- stays out of the timing.
         graph = None
-        if world == 1 and not args.no_graph:
+        if not args.no_graph:
             side = torch.cuda.Stream(device)
             side.wait_stream(torch.cuda.current_stream(device))
             with torch.cuda.stream(side):
@@ -592,9 +593,9 @@ def run_sweep(args, torch):
             torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        times = []
+        marks = []
         stream = torch.cuda.current_stream(device)
-        for _ in range(max(3, min(args.steps, 10))):
+        for _ in range(max(3, min(args.steps, 10))):  # queued back to back, read at the end
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
@@ -604,8 +605,9 @@ def run_sweep(args, torch):
                 for c in calls:
                     c()
             e1.record(stream)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1) / 1000.0)
+            marks.append((e0, e1))
+        torch.cuda.synchronize()
+        times = [e0.elapsed_time(e1) / 1000.0 for e0, e1 in marks]
         del graph
         sec = statistics.median(times)
         if world > 1:
@@ -615,7 +617,7 @@ def run_sweep(args, torch):
         results.append({"M": m, "ms_per_pass": 1000 * sec, "tflops": flops / sec / 1e12,
                         "pct_peak": 100 * flops / sec / 1e12 / (peak_burst * world),
                         "hbm_gbs": nbytes / sec / 1e9, "pct_hbm": 100 * nbytes / sec / 1e9 / (hbm * world),
-                        "projection_calls": len(calls), "cuda_graph": world == 1 and not args.no_graph})
+                        "projection_calls": len(calls), "cuda_graph": not args.no_graph})
     err = _lib.take_device_error(device)
     if rank == 0:
         print(json.dumps({"metric": "NF4 dequant-GEMM fwd+dX at Qwen2.5-7B shapes (configs[4])",
@@ -973,11 +975,14 @@ def main():
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
-    # ---- timed region: K steps, L2 flushed before each (outside the events)
+    # ---- timed region: K steps, L2 flushed before each (outside the events).  The
+    # steps are queued back to back and read once at the end: a host round trip
+    # per step would let the ranks' hosts drift apart, and on N GPUs every rank's
+    # all-reduce would then wait for the latest host's launch.
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    step_times = []
+    marks = []
     with ClockSampler(local) as clocks:
         for _ in range(args.steps):
             flush.zero_()
@@ -985,9 +990,9 @@ def main():
             e0.record(stream)
             run_step()
             e1.record(stream)
-            e1.synchronize()
-            step_times.append(e0.elapsed_time(e1) / 1000.0)
-    torch.cuda.synchronize()
+            marks.append((e0, e1))
+        torch.cuda.synchronize()
+    step_times = [e0.elapsed_time(e1) / 1000.0 for e0, e1 in marks]
     if dist is not None:
         dist.barrier()
     local_total = sum(step_times)
