@@ -553,14 +553,17 @@ def run_sweep(args, torch):
             else:
                 rows = sh.row1 - sh.row0
                 dy_loc = dy[:, sh.row0:sh.row1].contiguous()
-                buf = torch.empty((world * m, -(-n // world) + 64), device=device, dtype=torch.float16)
+                # Equal row shards (every sweep width divides by N): the ranks' Y
+                # blocks are gathered straight into one [N, m, rows] buffer, which is
+                # Y itself at m = 1 and Y after one column-block interleave otherwise.
+                assert n % world == 0 and rows == n // world
+                buf = torch.empty((world * m, rows), device=device, dtype=torch.float16)
 
                 def fwd(x=x, sh=sh, rows=rows, buf=buf):
-                    y = nf4_linear_raw(x, sh.packed, sh.state)
-                    pad = torch.zeros((m, buf.shape[1]), device=device, dtype=torch.float16)
-                    pad[:, :rows] = y
-                    dist.all_gather_into_tensor(buf, pad)
-                    return buf
+                    dist.all_gather_into_tensor(buf, nf4_linear_raw(x, sh.packed, sh.state))
+                    if m == 1:
+                        return buf.view(1, world * rows)
+                    return buf.view(world, m, rows).permute(1, 0, 2).reshape(m, world * rows)
 
                 def dxf(dy_loc=dy_loc, sh=sh):
                     return allreduce_sum(nf4_linear_raw(dy_loc, sh.packed, sh.state, transpose=True))

@@ -118,6 +118,14 @@ class _GatherColumns(torch.autograd.Function):
         ctx.sizes, ctx.rank = sizes, rank
         m = local.shape[0]
         width = max(sizes)
+        if all(w == width for w in sizes):
+            # Equal blocks: gathered as they are into [world, m, width], which is Y
+            # for one row and Y after one interleave of the column blocks otherwise.
+            buf = local.new_empty((world * m, width))
+            dist.all_gather_into_tensor(buf, local.contiguous(), group=group)
+            if m == 1:
+                return buf.view(1, world * width)
+            return buf.view(world, m, width).permute(1, 0, 2).reshape(m, world * width)
         buf = local.new_zeros((world * m, width))
         mine = local.new_zeros((m, width))
         mine[:, :local.shape[1]] = local
@@ -147,18 +155,24 @@ class _SumGradient(torch.autograd.Function):
         return grad, None
 
 
-def column_parallel(x, local_fn, n_total, group=None):
+def column_parallel(x, local_fn, n_total, group=None, sizes=None):
     """Y[M, N] = gather_r(local_fn(x)) with dX summed over ranks in the backward.
-    `local_fn` maps x to this rank's column block (a differentiable function)."""
-    world, _ = _world(group)
+    `local_fn` maps x to this rank's column block (a differentiable function).
+    `sizes` lists every rank's block width when the caller knows them; otherwise
+    they are exchanged (one small all-gather and a host read)."""
+    world, rank = _world(group)
     x_in = _SumGradient.apply(x, group)
     local = local_fn(x_in)
     lead = local.shape[:-1]
     local2d = local.reshape(-1, local.shape[-1])
-    sizes_t = torch.tensor([local2d.shape[1]], device=local.device)
-    gathered = [torch.zeros_like(sizes_t) for _ in range(world)]
-    dist.all_gather(gathered, sizes_t, group=group)
-    sizes = [int(s.item()) for s in gathered]
+    if sizes is None:
+        sizes_t = torch.tensor([local2d.shape[1]], device=local.device)
+        gathered = [torch.zeros_like(sizes_t) for _ in range(world)]
+        dist.all_gather(gathered, sizes_t, group=group)
+        sizes = [int(s.item()) for s in gathered]
+    sizes = list(sizes)
+    if len(sizes) != world or sizes[rank] != local2d.shape[1]:
+        raise ValueError(f"column block widths {sizes} do not match this rank's {local2d.shape[1]}")
     if sum(sizes) != n_total:
         raise ValueError(f"column blocks {sizes} do not add up to {n_total}")
     y = _GatherColumns.apply(local2d, sizes, group)
@@ -174,7 +188,15 @@ def nsplit_nf4_lora_linear(x, shard, lora_a, lora_b_rows, scaling, n_total, bias
     def local(xi):
         return nf4_lora_linear(xi, shard.packed, shard.state, lora_a, lora_b_rows, scaling, bias_rows)
 
-    return column_parallel(x, local, n_total, group)
+    world, rank = _world(group)
+    k_in = shard.state.shape[1]
+    sizes = None
+    if k_in % 64 == 0:
+        # Shards made by nf4_row_shard: every rank's rows follow from the shape.
+        bounds = [even_split(n_total, world, r, shard_align_rows(k_in)) for r in range(world)]
+        if bounds[rank] == (shard.row0, shard.row1):
+            sizes = [b1 - b0 for b0, b1 in bounds]
+    return column_parallel(x, local, n_total, group, sizes=sizes)
 
 
 # ----------------------------------------------------------------------------- vocabulary shards

@@ -73,7 +73,7 @@ def test_nf4_row_shards_are_exact_slices(n, k):
 
 
 # ------------------------------------------------------------------ column-parallel projection
-def _check_column_parallel(rank, m, n, k):
+def _check_column_parallel(rank, m, n, k, known):
     from soupsuck_b200.distributed import column_parallel, even_split
 
     torch.manual_seed(0)
@@ -81,15 +81,20 @@ def _check_column_parallel(rank, m, n, k):
     w = torch.randn(n, k, dtype=torch.float64)
     dy = torch.randn(m, n, dtype=torch.float64)
     r0, r1 = even_split(n, WORLD, rank, 64)
+    sizes = [b - a for a, b in (even_split(n, WORLD, r, 64) for r in range(WORLD))] if known else None
     x = x_full.clone().requires_grad_()
-    y = column_parallel(x, lambda xi: xi @ w[r0:r1].t(), n)
+    y = column_parallel(x, lambda xi: xi @ w[r0:r1].t(), n, sizes=sizes)
     y.backward(dy)
+    assert y.shape == (m, n)
     assert torch.allclose(y, x_full @ w.t())
     assert torch.allclose(x.grad, dy @ w)
 
 
-def test_column_parallel_gathers_y_and_sums_dx():
-    _run(_check_column_parallel, 37, 300, 64)
+# Unequal blocks (300 = 128 + 172: padded gather), equal blocks at one and at
+# several rows (gathered as they are), widths passed by the caller.
+@pytest.mark.parametrize("m,n,known", [(37, 300, False), (37, 256, False), (1, 256, False), (5, 256, True)])
+def test_column_parallel_gathers_y_and_sums_dx(m, n, known):
+    _run(_check_column_parallel, m, n, 64, known)
 
 
 # ------------------------------------------------------------------ vocabulary-shard CE merge
