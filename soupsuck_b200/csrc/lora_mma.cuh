@@ -562,21 +562,24 @@ __global__ void prepare_kernel(const void* __restrict__ a, int adt, const void* 
                                int bdt, int r, int64_t K, int64_t N, __half* __restrict__ a16,
                                __half* __restrict__ at16, __half* __restrict__ b16,
                                __half* __restrict__ bt16) {
-  const int64_t na = static_cast<int64_t>(r) * K;
-  const int64_t total = na + static_cast<int64_t>(r) * N;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+  // One index range per output array, so every array is written in order
+  // (coalesced); the small inputs are read through the caches.  Sizes fit 32 bits.
+  const uint32_t rr = static_cast<uint32_t>(r), kk = static_cast<uint32_t>(K), nn = static_cast<uint32_t>(N);
+  const uint32_t na = rr * kk, nbv = rr * nn;
+  const uint32_t total = 2 * na + 2 * nbv;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     if (i < na) {
-      const int64_t j = i / K, k = i % K;
-      const __half v = __float2half_rn(ld_as_f32(a, adt, i));
-      if (a16) a16[i] = v;
-      if (at16) at16[k * r + j] = v;
+      if (a16) a16[i] = __float2half_rn(ld_as_f32(a, adt, i));
+    } else if (i < 2 * na) {
+      const uint32_t e = i - na, k = e / rr, j = e - k * rr;  // at16[k][j] = a[j][k]
+      if (at16) at16[e] = __float2half_rn(ld_as_f32(a, adt, static_cast<int64_t>(j) * kk + k));
+    } else if (i < 2 * na + nbv) {
+      const uint32_t e = i - 2 * na;
+      if (b16) b16[e] = __float2half_rn(ld_as_f32(b, bdt, e));
     } else {
-      const int64_t ib = i - na;
-      const int64_t n = ib / r, j = ib % r;
-      const __half v = __float2half_rn(ld_as_f32(b, bdt, ib));
-      if (b16) b16[ib] = v;
-      if (bt16) bt16[j * N + n] = v;
+      const uint32_t e = i - 2 * na - nbv, j = e / nn, n = e - j * nn;  // bt16[j][n] = b[n][j]
+      if (bt16) bt16[e] = __float2half_rn(ld_as_f32(b, bdt, static_cast<int64_t>(n) * rr + j));
     }
   }
 }
@@ -584,29 +587,40 @@ __global__ void prepare_kernel(const void* __restrict__ a, int adt, const void* 
 // Two adapters of one input as one rank-2r adapter: a1, a2 [r, K] and b1, b2 [N, r]
 // (dtype adt / bdt) -> a_cat [2r, K] (a1 over a2), at_cat [K, 2r], b_bd [2N, 2r]
 // = [[b1, 0], [0, b2]] and bt_bd [2r, 2N] (its transpose), fp16, zero blocks
-// written too.  One pass over every output element.
+// written too.  One index range per output array (each written in order).
 __global__ void pair_prepare_kernel(const void* __restrict__ a1, const void* __restrict__ a2, int adt,
                                     const void* __restrict__ b1, const void* __restrict__ b2, int bdt, int r,
                                     int64_t K, int64_t N, __half* __restrict__ a_cat, __half* __restrict__ at_cat,
                                     __half* __restrict__ b_bd, __half* __restrict__ bt_bd) {
-  const int64_t na = 2 * static_cast<int64_t>(r) * K;
-  const int64_t nb = 2 * N * 2 * static_cast<int64_t>(r);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < na + nb; i += stride) {
+  const uint32_t rr = static_cast<uint32_t>(r), r2 = 2 * rr, kk = static_cast<uint32_t>(K);
+  const uint32_t n2 = 2 * static_cast<uint32_t>(N), nn = static_cast<uint32_t>(N);
+  const uint32_t na = r2 * kk, nbv = n2 * r2;
+  const uint32_t total = 2 * na + 2 * nbv;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  // a_cat[j][k] for j in [0, 2r); b_bd[row][c] is b1 / b2 on the diagonal blocks.
+  auto a_val = [&](uint32_t j, uint32_t k) -> __half {
+    const bool second = j >= rr;
+    return __float2half_rn(ld_as_f32(second ? a2 : a1, adt, static_cast<int64_t>(second ? j - rr : j) * kk + k));
+  };
+  auto b_val = [&](uint32_t row, uint32_t c) -> __half {
+    const bool row2 = row >= nn, col2 = c >= rr;
+    if (row2 != col2) return __float2half_rn(0.0f);
+    return __float2half_rn(ld_as_f32(row2 ? b2 : b1, bdt, static_cast<int64_t>(row2 ? row - nn : row) * rr +
+                                                              (col2 ? c - rr : c)));
+  };
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     if (i < na) {
-      const int64_t j = i / K, k = i % K;  // j in [0, 2r)
-      const bool second = j >= r;
-      const __half v = __float2half_rn(ld_as_f32(second ? a2 : a1, adt, (second ? j - r : j) * K + k));
-      a_cat[i] = v;
-      at_cat[k * 2 * r + j] = v;
+      const uint32_t j = i / kk;
+      a_cat[i] = a_val(j, i - j * kk);
+    } else if (i < 2 * na) {
+      const uint32_t e = i - na, k = e / r2;
+      at_cat[e] = a_val(e - k * r2, k);
+    } else if (i < 2 * na + nbv) {
+      const uint32_t e = i - 2 * na, row = e / r2;
+      b_bd[e] = b_val(row, e - row * r2);
     } else {
-      const int64_t ib = i - na;
-      const int64_t n2 = ib / (2 * r), c = ib % (2 * r);  // row of b_bd, column in [0, 2r)
-      const bool row2 = n2 >= N, col2 = c >= r;
-      __half v = __float2half_rn(0.0f);
-      if (row2 == col2) v = __float2half_rn(ld_as_f32(row2 ? b2 : b1, bdt, (row2 ? n2 - N : n2) * r + (col2 ? c - r : c)));
-      b_bd[ib] = v;
-      bt_bd[c * 2 * N + n2] = v;
+      const uint32_t e = i - 2 * na - nbv, c = e / n2;
+      bt_bd[e] = b_val(e - c * n2, c);
     }
   }
 }
@@ -651,10 +665,15 @@ inline int launch_reduce2(dim3 grid, const __half* P, int64_t ldp, const __half*
 // Warps for u: (m16 tile mi, group nq of RH/16 n8 tiles, column half kh), the two
 // column halves added in fixed order through shared memory.  DB = false: u only
 // (the forward's Z = X.A^T for long rows), without Pt, dB or its partials.
+// Three ring slots (two tiles in flight): 63 KB of shared memory at RH = 16, so
+// three CTAs (24 warps) share an SM.  The kernel waits on shared-memory and MMA
+// latency (ldmatrix -> mma chains) more than on bytes in flight.
+constexpr int kDualStages = 3;
+
 template <int RH>
 struct DualSmem {
   static constexpr int kStage = Red2Smem<RH>::kStage;
-  static constexpr int kRing = kRedStages * kStage;
+  static constexpr int kRing = kDualStages * kStage;
   static constexpr int kBtBytes = RH * kRedCols * 2;           // the CTA's Bt block
   static constexpr int kXchBytes = 2 * 4 * 32 * (RH / 4) * 4;  // two tiles' column-half partials
   static constexpr int kBytes = kRing + kBtBytes + kXchBytes;
@@ -682,7 +701,7 @@ __global__ void __launch_bounds__(256) dual_kernel(
   float* xch = reinterpret_cast<float*>(dual_smem + S::kRing + S::kBtBytes);
 
   auto issue = [&](int tile) {
-    const int slot = tile % kRedStages;
+    const int slot = tile % kDualStages;
     const uint32_t qs = sbase + slot * S::kStage;
     const uint32_t ps = qs + Red2Smem<RH>::kQBytes;
     const int64_t r0 = mb + static_cast<int64_t>(tile) * kRedRows;
@@ -718,7 +737,7 @@ __global__ void __launch_bounds__(256) dual_kernel(
     for (int n = 0; n < 4; ++n) acc[i][n][0] = acc[i][n][1] = acc[i][n][2] = acc[i][n][3] = 0.0f;
 
 #pragma unroll
-  for (int s = 0; s < kRedStages - 1; ++s) {
+  for (int s = 0; s < kDualStages - 1; ++s) {
     if (s < ntiles) issue(s);
     cp_async_commit();
   }
@@ -726,11 +745,11 @@ __global__ void __launch_bounds__(256) dual_kernel(
   const int mi = warp & 1, nq = (warp >> 1) & 1, kh = warp >> 2;
   const int64_t ublock = static_cast<int64_t>(blockIdx.x) * ldq;
   for (int tile = 0; tile < ntiles; ++tile) {
-    cp_async_wait<kRedStages - 2>();
+    cp_async_wait<kDualStages - 2>();
     __syncthreads();
-    if (tile + kRedStages - 1 < ntiles) issue(tile + kRedStages - 1);
+    if (tile + kDualStages - 1 < ntiles) issue(tile + kDualStages - 1);
     cp_async_commit();
-    const int slot = tile % kRedStages;
+    const int slot = tile % kDualStages;
     const uint32_t qs = sbase + slot * S::kStage;
     const uint32_t ps = qs + Red2Smem<RH>::kQBytes;
     // dB += Pt[:, tile rows] . Q[tile rows, warp's 32 columns]
@@ -896,15 +915,30 @@ struct DualPlan {
   size_t partial_bytes, upart_bytes;
 };
 
+// The split count is chosen for whole waves of dual_kernel (three CTAs per SM at
+// RH = 16, two at RH = 32): cost = waves x (row tiles per CTA + one for the
+// CTA's partial-sum write), fewest splits on ties.
 inline DualPlan dual_plan(int64_t m, int64_t w, int rh) {
   DualPlan d{};
   d.ldq = (m + 15) / 16 * 16;
-  int s = reduce2_splits(d.ldq, w);
-  int64_t rps = (d.ldq + s - 1) / s;
-  rps = (rps + kRedRows - 1) / kRedRows * kRedRows;
+  d.nblocks = static_cast<int>((w + kRedCols - 1) / kRedCols);
+  const int64_t slots = (rh == 16 ? 3 : 2) * static_cast<int64_t>(device_sm_count());
+  const int64_t max_s = std::max<int64_t>(1, std::min<int64_t>(4096, (d.ldq + 63) / 64));
+  int64_t best_rps = d.ldq, best_cost = INT64_MAX;
+  for (int64_t s = 1; s <= max_s; ++s) {
+    int64_t rps = (d.ldq + s - 1) / s;
+    rps = (rps + kRedRows - 1) / kRedRows * kRedRows;
+    const int64_t splits = (d.ldq + rps - 1) / rps;
+    const int64_t waves = (d.nblocks * splits + slots - 1) / slots;
+    const int64_t cost = waves * (rps / kRedRows + 1);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best_rps = rps;
+    }
+  }
+  const int64_t rps = best_rps;
   d.rows_per_split = rps;
   d.splits = static_cast<int>((d.ldq + rps - 1) / rps);
-  d.nblocks = static_cast<int>((w + kRedCols - 1) / kRedCols);
   d.partial_bytes = (static_cast<size_t>(d.splits) * rh * w * sizeof(float) + 255) / 256 * 256;
   d.upart_bytes = static_cast<size_t>(d.nblocks) * d.ldq * rh * sizeof(float);
   return d;
@@ -1113,7 +1147,8 @@ int sb_lora_prepare(const void* a, int a_dtype, const void* b, int b_dtype, int 
   SB_REQUIRE(r > 0 && k > 0 && n > 0, "expected positive sizes");
   SB_REQUIRE((a_dtype == SB_F16 || a_dtype == SB_F32) && (b_dtype == SB_F16 || b_dtype == SB_F32), "bad dtype");
   SB_REQUIRE(a && b, "NULL pointer argument");
-  const int64_t total = static_cast<int64_t>(r) * (k + n);
+  SB_REQUIRE(2 * static_cast<int64_t>(r) * (k + n) < (int64_t(1) << 31), "LoRA factors too large");
+  const int64_t total = 2 * static_cast<int64_t>(r) * (k + n);
   const int64_t blocks = (total + 255) / 256;
   const int grid = static_cast<int>(blocks < 4096 ? blocks : 4096);
   sb::lora::prepare_kernel<<<grid, 256, 0, sb::as_stream(stream)>>>(
@@ -1129,7 +1164,8 @@ int sb_lora_prepare_pair(const void* a1, const void* a2, int a_dtype, const void
   SB_REQUIRE(r > 0 && k > 0 && n > 0, "expected positive sizes");
   SB_REQUIRE((a_dtype == SB_F16 || a_dtype == SB_F32) && (b_dtype == SB_F16 || b_dtype == SB_F32), "bad dtype");
   SB_REQUIRE(a1 && a2 && b1 && b2 && a_cat && at_cat && b_bd && bt_bd, "NULL pointer argument");
-  const int64_t total = 2 * static_cast<int64_t>(r) * k + 4 * n * static_cast<int64_t>(r);
+  const int64_t total = 4 * static_cast<int64_t>(r) * k + 8 * n * static_cast<int64_t>(r);
+  SB_REQUIRE(total < (int64_t(1) << 31), "LoRA factors too large");
   const int64_t blocks = (total + 255) / 256;
   const int grid = static_cast<int>(blocks < 4096 ? blocks : 4096);
   sb::lora::pair_prepare_kernel<<<grid, 256, 0, sb::as_stream(stream)>>>(
