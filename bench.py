@@ -978,6 +978,10 @@ def main():
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
+    # One untimed flush + step: the flush buffer's first write maps its pages, and
+    # on N GPUs a first step behind it would make the other ranks' all-reduce wait.
+    flush.zero_()
+    run_step()
     # ---- timed region: K steps, L2 flushed before each (outside the events).  The
     # steps are queued back to back and read once at the end: a host round trip
     # per step would let the ranks' hosts drift apart, and on N GPUs every rank's
@@ -987,6 +991,11 @@ def main():
     torch.cuda.synchronize()
     marks = []
     with ClockSampler(local) as clocks:
+        if dist is not None:
+            # The ranks' hosts leave the barrier at different times; one small
+            # all-reduce queued ahead of the first step lines the GPUs up, so the
+            # first step's in-graph all-reduce does not wait for the latest host.
+            dist.all_reduce(torch.zeros(1, device=device))
         for _ in range(args.steps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1000,10 +1009,21 @@ def main():
         dist.barrier()
     local_total = sum(step_times)
     total = local_total
+    rank_steps = None
     if dist is not None:
         tt = torch.tensor([local_total], device=device, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         total = float(tt.item())
+        # Every rank's own mean / fastest / slowest step (ms), the slowest step's
+        # index and the median SM clock: with the all-reduce inside each step,
+        # ranks that wait for a slower one show it in their mean.
+        mhz = clocks.summary()["sm_mhz"]
+        mine = torch.tensor([1000 * local_total / args.steps, 1000 * min(step_times), 1000 * max(step_times),
+                             float(step_times.index(max(step_times))), float(mhz) if mhz is not None else -1.0],
+                            device=device, dtype=torch.float64)
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        rank_steps = [[round(float(x), 4) for x in e.tolist()] for e in every]
     sec_per_step = total / args.steps
     flops = step_flops(t) * world
     value = flops / sec_per_step / 1e12
@@ -1131,6 +1151,9 @@ def main():
         "clocks": clocks.summary(),
         "device_error": dev_err,
     }
+    if rank_steps is not None:
+        line["rank_step_ms"] = {"fields": ["mean ms", "min ms", "max ms", "index of the slowest step",
+                                           "median SM MHz"], "ranks": rank_steps}
     if ce is not None:
         line["ce"] = ce
     if cpu is not None:
